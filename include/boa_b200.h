@@ -1,0 +1,149 @@
+/*
+ * boa_b200.h — C-ABI of libboa_b200.so, the B200 (sm_100a) compress/decompress
+ * hot path of BoaConstrictor.
+ *
+ * Conventions (every entry point):
+ *   - returns BOA_OK (0) or a BOA_ERR_* code; boa_last_error() gives a message
+ *     for the calling thread;
+ *   - pointers named d_* are device pointers on the handle's device, h_* /
+ *     host_* are host pointers; sizes are in elements unless named *_bytes;
+ *   - `stream` is a cudaStream_t passed as void*; work is stream-ordered and
+ *     nothing synchronises the device.  Calls that return host data
+ *     synchronise only `stream`.
+ *   - no torch or C++ types cross this boundary.
+ *
+ * Reference interfaces replaced (paths relative to the reference project root):
+ *   boa_rc_*      : pybind11 class RangeCoderBatch, gpu_range_coder.py:212-324,
+ *                   wrapped by gpu.queue.RangeCoderBatch, gpu_range_coder.py:488-550
+ *   boa_model_*   : BoaConstrictor / BoaBytePredictor.step, model.py:5,83-131,
+ *                   weights in the order of portability_solved_cpp/convert_boa_weights.py:16-135
+ *   boa_codec_*   : the per-byte step loops compress_GPU / decompress_GPU,
+ *                   codec.py:11-86 and codec.py:89-151 (model step + softmax +
+ *                   coder step per byte), fused into one persistent kernel
+ */
+#ifndef BOA_B200_H
+#define BOA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BOA_API __attribute__((visibility("default")))
+
+#define BOA_ABI_VERSION 1
+
+#define BOA_OK 0
+#define BOA_ERR_ARG 1        /* invalid argument / shape (reference: std::runtime_error) */
+#define BOA_ERR_CUDA 2       /* a CUDA runtime call failed */
+#define BOA_ERR_OVERFLOW 3   /* a compressed stream needed more words than its pitch */
+#define BOA_ERR_TIMEOUT 4    /* a bounded device-side wait gave up */
+#define BOA_ERR_UNSUPPORTED 5
+
+/* Frequency-table quantisers. */
+#define BOA_QUANT_REF 0  /* fp32 probabilities -> reference build_cdf_fast (gpu_range_coder.py:57-79) */
+#define BOA_QUANT_BQ 1   /* fp32 logits -> this build's integer quantiser (no reference counterpart) */
+
+/* Projection weight formats for the model kernel. */
+#define BOA_WEIGHTS_TF32 0  /* fp32 weights, tf32 tensor-core products, fp32 accumulation */
+#define BOA_WEIGHTS_BF16 1  /* bf16 weights and activations, fp32 accumulation and state */
+
+BOA_API const char* boa_last_error(void);
+BOA_API int boa_abi_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Batched range coder (gpu_range_coder.py:212-324).                        */
+/* ------------------------------------------------------------------------ */
+typedef struct boa_rc_batch boa_rc_batch;
+
+/* RangeCoderBatch(int N, int K, int pitch) (gpu_range_coder.py:219-230).
+ * precision: 24 reproduces the reference coder bit for bit (with
+ * BOA_QUANT_REF); 16 is the north-star table total.  Allocates the per-stream
+ * coder state and N*pitch_words output words on `device`. */
+BOA_API int boa_rc_create(boa_rc_batch** out, int n_streams, int k_symbols, int pitch_words,
+                          int precision, int quantiser, int device);
+/* ~RangeCoderBatch (gpu_range_coder.py:231-236). */
+BOA_API int boa_rc_destroy(boa_rc_batch* b);
+BOA_API int boa_rc_info(const boa_rc_batch* b, int* n_streams, int* k_symbols, int* pitch_words,
+                        int* precision, int* quantiser);
+/* load_compressed_from_host (gpu_range_coder.py:237-253): host_words is
+ * [n_streams, pitch_words] (zero padded), host_sizes[n_streams] in words. */
+BOA_API int boa_rc_load(boa_rc_batch* b, const uint32_t* host_words, const int32_t* host_sizes, void* stream);
+/* set_sizes_from_host (gpu_range_coder.py:259-264). */
+BOA_API int boa_rc_set_sizes(boa_rc_batch* b, const int32_t* host_sizes, void* stream);
+/* get_sizes_host (gpu_range_coder.py:254-258); reports BOA_ERR_OVERFLOW if a
+ * stream ran past its pitch. */
+BOA_API int boa_rc_get_sizes(boa_rc_batch* b, int32_t* host_sizes, void* stream);
+/* get_compressed_host (gpu_range_coder.py:278-292), as one [n, pitch] block. */
+BOA_API int boa_rc_get_words(boa_rc_batch* b, uint32_t* host_words, void* stream);
+/* Device addresses of the [n, pitch] word block and the size vector. */
+BOA_API int boa_rc_device_buffers(boa_rc_batch* b, uint32_t** d_words, int32_t** d_sizes);
+/* encode_step_from_device (gpu_range_coder.py:265-272): one symbol per active
+ * stream.  d_rows is [n, K] fp32: probabilities for BOA_QUANT_REF, logits for
+ * BOA_QUANT_BQ.  d_mask (u8, may be NULL) skips streams with mask 0. */
+BOA_API int boa_rc_encode_step(boa_rc_batch* b, const int32_t* d_symbols, const float* d_rows,
+                               const uint8_t* d_mask, void* stream);
+/* finalize (gpu_range_coder.py:273-277). */
+BOA_API int boa_rc_finalize(boa_rc_batch* b, void* stream);
+/* init_decoder_from_current_bytes (gpu_range_coder.py:293-297). */
+BOA_API int boa_rc_init_decoder(boa_rc_batch* b, void* stream);
+/* decode_step_to_device (gpu_range_coder.py:298-305). */
+BOA_API int boa_rc_decode_step(boa_rc_batch* b, const float* d_rows, int32_t* d_out_symbols,
+                               const uint8_t* d_mask, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* BoaConstrictor model (model.py:5-134).                                   */
+/* ------------------------------------------------------------------------ */
+typedef struct boa_model boa_model;
+
+/* Build the device model from fp32 weights in the flat order written by
+ * portability_solved_cpp/convert_boa_weights.py:16-135 (in_proj/out_proj bias
+ * slots present and zero).  d_state 16, d_conv 4, expand 2, dt_rank
+ * ceil(d_model/16) as in mamba_ssm.Mamba(d_model) (model.py:47). */
+BOA_API int boa_model_create(boa_model** out, int d_model, int n_layers, int vocab,
+                             const float* host_flat_weights, size_t n_floats, int weight_format,
+                             int device);
+BOA_API int boa_model_destroy(boa_model* m);
+/* Bytes of device workspace (recurrent state + bookkeeping) that one
+ * boa_codec_* / boa_model_logits call over n_chunks streams needs. */
+BOA_API size_t boa_model_workspace_bytes(const boa_model* m, int n_chunks);
+
+/* Reference-shaped single step: the streaming state of init_stream/step
+ * (model.py:104-117) lives in d_workspace (zero it to start a stream).
+ * d_tokens [n] int32 -> d_logits [n, vocab] fp32. */
+BOA_API int boa_model_step(boa_model* m, int n, const int32_t* d_tokens, float* d_logits,
+                           void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* n streams x n_steps tokens [n, n_steps] (int32), from zero state, all
+ * logits out [n, n_steps, vocab] (fp32).  Diagnostic/parity entry point. */
+BOA_API int boa_model_logits(boa_model* m, int n, int n_steps, const int32_t* d_tokens,
+                             float* d_logits, void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Fused codec loops (codec.py:11-86 compress_GPU, codec.py:89-151           */
+/* decompress_GPU): model step -> quantiser -> range coder for every byte,   */
+/* all chunks of the batch in flight, no host round trip per byte.           */
+/* ------------------------------------------------------------------------ */
+
+/* Chunk i holds d_lens[i] >= 1 bytes at d_bytes + i*in_pitch.  Byte 0 is not
+ * coded (the container stores it raw, codec.py:38); bytes 1..len-1 are coded
+ * with the BQ quantiser at `precision`.  Writes d_words [n, pitch_words] and
+ * d_sizes[n] (words).  d_workspace must hold boa_model_workspace_bytes(). */
+BOA_API int boa_codec_encode(boa_model* m, int n_chunks, const uint8_t* d_bytes, int64_t in_pitch,
+                             const int32_t* d_lens, uint32_t* d_words, int pitch_words, int32_t* d_sizes,
+                             int precision, void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* Inverse of boa_codec_encode: d_out [n, out_pitch] receives the chunks
+ * (byte 0 from d_first_bytes). */
+BOA_API int boa_codec_decode(boa_model* m, int n_chunks, const uint32_t* d_words, int pitch_words,
+                             const int32_t* d_sizes, const int32_t* d_lens, const uint8_t* d_first_bytes,
+                             uint8_t* d_out, int64_t out_pitch, int precision, void* d_workspace,
+                             size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BOA_B200_H */
