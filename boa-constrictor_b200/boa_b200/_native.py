@@ -26,6 +26,7 @@ BOA_QUANT_BQ = 1
 
 BOA_WEIGHTS_TF32 = 0
 BOA_WEIGHTS_BF16 = 1
+BOA_WEIGHTS_F16 = 2
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -51,6 +52,8 @@ SIGNATURES = {
     "boa_model_create": [_P, _I, _I, _I, _P, _SZ, _I, _I],
     "boa_model_destroy": [_P],
     "boa_model_workspace_bytes": [_P, _I],
+    "boa_model_info": [_P, _P, _P, _P, _P, _P],
+    "boa_diag_gemm": [_I, _I, _I, _P, _P, _P, _I],
     "boa_model_step": [_P, _I, _P, _P, _P, _SZ, _P],
     "boa_model_logits": [_P, _I, _I, _P, _P, _P, _SZ, _P],
     "boa_codec_encode": [_P, _I, _P, _I64, _P, _P, _I, _P, _I, _P, _SZ, _P],

@@ -1,26 +1,1049 @@
-// Model entry points (placeholder until the fused step kernel lands).
+// BoaConstrictor model + fused codec loop for sm_100a.
+//
+// What it computes, per byte and per chunk (paths relative to the reference
+// project root):
+//   h = Emb[prev]                                             model.py:111
+//   per block (model.py:57-65):  u = LN1(h)
+//     Mamba step (mamba_ssm.Mamba.step; op order also in
+//     portability_solved_cpp/boa_gpu.hpp:188-218, mamba_kernels.cu:158-192,264-338):
+//       [x,z] = u W_in^T ; conv shift + SiLU -> xc ; [dtr,B,C] = xc W_x^T ;
+//       dt = softplus(dtr W_dt^T + b_dt) ; h_n = exp(dt A_n) h_n + dt B_n xc ;
+//       y = C.h + D xc ; y *= SiLU(z) ; o = y W_out^T
+//     v = LN2(o) ; h += W2 GELU(W1 v + b1) + b2                 model.py:52-56
+//   logits = W_h2 ReLU(W_h1 h + b_h1) + b_h2                    model.py:90-95
+//   then quantiser + range coder (codec.py:63-76 / 131-141).
+//
+// Design (B200-first, not a port): one persistent CTA owns CT chunks and runs
+// every timestep of every layer for them; CTAs never talk to each other
+// because the whole step is row-local per chunk.  Roles inside the CTA:
+//   warp 0      streams every projection weight tile (pre-packed 16 KB SW128
+//               images, in consumption order) through a shared-memory ring
+//               with bulk async copies;
+//   warp 1      allocates TMEM and issues tcgen05.mma: weights are the A
+//               operand (M = 128 output features per tile), the chunks'
+//               activations the B operand (N = CT), accumulators in TMEM;
+//   warps 2-17  (512 threads) run the LayerNorms, conv/scan/gate, MLP and head
+//               epilogues straight out of TMEM, write the next B operand into
+//               shared memory, and run quantiser + range coder (a warp per chunk).
+// The recurrent state (conv window + SSM state, fp32) streams from HBM once
+// per layer per byte; everything else stays on chip.  Every accumulator column
+// depends only on its own chunk and the weights, in a fixed K order, so the
+// probabilities do not depend on batch composition, grid size or GPU.
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+#include <cstring>
+#include <cmath>
+#include <string>
+#include <vector>
+
 #include "boa_b200.h"
 #include "capi_util.h"
+#include "rc_device.cuh"
+#include "tc_sm100.cuh"
+
+namespace boa {
+
+constexpr int kTileBytes = 16384;      // one A tile: 128 rows x 128 bytes
+constexpr int kComputeThreads = 512;   // warps 2..17
+constexpr int kThreads = 576;
+constexpr int kStages = 4;             // weight ring depth
+constexpr int kCT = 16;                // chunks per CTA (MMA N)
+constexpr long long kWaitBudget = 4000000000LL;  // SM clock cycles per bounded wait (~2 s)
+
+enum StepMode : int { MODE_ENCODE = 0, MODE_DECODE = 1, MODE_LOGITS = 2 };
+
+// Per-layer small parameters (fp32), packed by the host in this order.
+template <int D>
+struct LayerParams {
+  static constexpr int E = 2 * D, F = 4 * D;
+  static constexpr int ln1w = 0, ln1b = D, convw = 2 * D, convb = convw + 4 * E, dtb = convb + E,
+                       A2 = dtb + E, Dp = A2 + 16 * E, ln2w = Dp + E, ln2b = ln2w + D, b1 = ln2b + D,
+                       b2 = b1 + F, stride = b2 + D;
+};
+
+static inline int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+// Projection tile counts per step (must match the kernel's consumption order).
+struct TilePlan {
+  int per, kD, kE, kF, mtE, mtD, mtF;
+  int t_in, t_xp, t_dt, t_out, t_ff1, t_ff2, t_h0, t_h2, per_layer, per_step;
+};
+static TilePlan make_plan(int D, int L, int kind) {
+  TilePlan p{};
+  p.per = kind == 0 ? 32 : 64;
+  const int E = 2 * D, F = 4 * D;
+  p.kD = D / p.per; p.kE = E / p.per; p.kF = F / p.per;
+  p.mtE = E / 128; p.mtD = cdiv(D, 128); p.mtF = F / 128;
+  p.t_in = 2 * p.mtE * p.kD; p.t_xp = p.kE; p.t_dt = p.mtE; p.t_out = p.mtD * p.kE;
+  p.t_ff1 = p.mtF * p.kD; p.t_ff2 = p.mtD * p.kF; p.t_h0 = p.mtD * p.kD; p.t_h2 = 2 * p.kD;
+  p.per_layer = p.t_in + p.t_xp + p.t_dt + p.t_out + p.t_ff1 + p.t_ff2;
+  p.per_step = p.per_layer * L + p.t_h0 + p.t_h2;
+  return p;
+}
+
+struct StepArgs {
+  int mode;                 // StepMode
+  int n_layers;
+  int vocab;
+  int n_chunks;
+  int n_steps;              // logits mode: tokens per stream
+  int fresh;                // 1: first step starts from zero state (no state loads)
+  int precision;
+  int tiles_per_step;
+  // encode input
+  const uint8_t* bytes; long long in_pitch;
+  const int32_t* lens;
+  // decode input / output
+  const uint32_t* words_in; const int32_t* sizes_in; const uint8_t* first_bytes;
+  uint8_t* out; long long out_pitch;
+  // encode output
+  uint32_t* words; int pitch_words; int32_t* sizes;
+  // logits mode
+  const int32_t* tokens; float* logits;
+  // model
+  const uint8_t* wtiles; const float* params;
+  float4* conv_state; float4* ssm_state;
+  uint32_t* err;
+};
+
+// ------------------------------ device math ---------------------------------
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+__device__ __forceinline__ float gelu_f(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
+__device__ __forceinline__ void cbar_sync() {   // named barrier over the 512 compute threads
+  asm volatile("bar.sync 1, 512;" ::: "memory");
+}
+
+// Shared-memory carve-up (dynamic smem, base rounded up to 1024 bytes).
+template <int D, int KIND>
+struct Smem {
+  static constexpr int CT = kCT;
+  static constexpr int EB = tc::OpKind<KIND>::kElemBytes;
+  static constexpr int F = 4 * D;
+  static constexpr int RING = kStages * kTileBytes;
+  static constexpr int BBUF = CT * F * EB;                  // largest K is F
+  static constexpr int HRES = CT * D * 4;
+  static constexpr int SCR = CT * (D > 256 ? D : 256) * 4;  // LN2 input / logits
+  static constexpr int DBCB = CT * 64 * 4;
+  static constexpr int o_ring = 0;
+  static constexpr int o_bbuf = o_ring + RING;
+  static constexpr int o_hres = o_bbuf + BBUF;
+  static constexpr int o_scr = o_hres + HRES;
+  static constexpr int o_dbc = o_scr + SCR;
+  static constexpr int o_enc = o_dbc + DBCB;                 // RcEnc / RcDec [CT]
+  static constexpr int o_prev = o_enc + CT * 32;
+  static constexpr int o_bars = o_prev + CT * 4;             // full[S], empty[S], mma, act, drain
+  static constexpr int o_misc = o_bars + (2 * kStages + 3) * 8;
+  static constexpr int TOTAL = o_misc + 64;
+  static constexpr int ALLOC = TOTAL + 1024;
+};
+
+// -------------------------------- the kernel --------------------------------
+template <int D, int KIND>
+__global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant__ StepArgs a) {
+  constexpr int CT = kCT;
+  constexpr int E = 2 * D, R = (D + 15) / 16, DBC = R + 32, F = 4 * D;
+  constexpr int PER = 128 / tc::OpKind<KIND>::kElemBytes;
+  constexpr int kD = D / PER, kE = E / PER, kF = F / PER;
+  constexpr int MT_E = E / 128, MT_D = (D + 127) / 128, MT_F = F / 128;
+  constexpr int COL_X = 0, COL_Z = MT_E * CT, COL_XP = 2 * MT_E * CT, COL_DT = COL_XP + CT;
+  static_assert(COL_DT + MT_E * CT <= 512, "TMEM budget");
+  static_assert(MT_F * CT <= 512, "TMEM budget (ff.0)");
+  static_assert(R <= PER && DBC <= 64, "x_proj outputs must fit one tile / one K slice");
+  static_assert(D % 32 == 0 && D >= 64, "d_model");
+  using S = Smem<D, KIND>;
+  using LP = LayerParams<D>;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem + S::o_ring;
+  uint8_t* bbuf = smem + S::o_bbuf;
+  float* hres = reinterpret_cast<float*>(smem + S::o_hres);
+  float* scr = reinterpret_cast<float*>(smem + S::o_scr);
+  float* dbc = reinterpret_cast<float*>(smem + S::o_dbc);
+  int32_t* prev = reinterpret_cast<int32_t*>(smem + S::o_prev);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::o_bars);
+  uint64_t* empty = full + kStages;
+  uint64_t* mma_bar = empty + kStages;
+  uint64_t* act_bar = mma_bar + 1;
+  uint64_t* drain_bar = act_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::o_misc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::o_misc + 4);
+  int* nsteps_sh = reinterpret_cast<int*>(smem + S::o_misc + 8);
+  volatile int* cons_sh = reinterpret_cast<volatile int*>(smem + S::o_misc + 12);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int c0 = blockIdx.x * CT;
+  const int mode = a.mode;
+  const int L = a.n_layers;
+  const int V = a.vocab;
+  const float* P = a.params;
+  const long long o_bh0 = (long long)LP::stride * L;
+  const long long o_bh2 = o_bh0 + D;
+  const long long o_emb = o_bh2 + 256;
+
+  // ------------------------------- setup -------------------------------
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
+    tc::mbar_init(mma_bar, 1);
+    tc::mbar_init(act_bar, kComputeThreads);
+    tc::mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    *cons_sh = 0;
+    int ns = 0;
+    if (mode == MODE_LOGITS) {
+      ns = a.n_steps;
+    } else {
+      for (int n = 0; n < CT; ++n) {
+        const int c = c0 + n;
+        if (c < a.n_chunks) ns = max(ns, a.lens[c] - 1);
+      }
+    }
+    *nsteps_sh = ns;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, 512);
+    tc::tmem_relinquish();
+  }
+  if (tid >= 64 && tid < 64 + CT) {
+    const int n = tid - 64;
+    const int c = c0 + n;
+    int p0 = 0;
+    if (c < a.n_chunks) {
+      if (mode == MODE_ENCODE) {
+        p0 = a.bytes[(long long)c * a.in_pitch];
+        rc_enc_reset(reinterpret_cast<RcEnc*>(smem + S::o_enc)[n]);
+      } else if (mode == MODE_DECODE) {
+        p0 = a.first_bytes[c];
+        int nw = a.sizes_in[c];
+        nw = nw < 0 ? 0 : (nw > a.pitch_words ? a.pitch_words : nw);
+        rc_dec_reset(reinterpret_cast<RcDec*>(smem + S::o_enc)[n], a.words_in + (long long)c * a.pitch_words, nw);
+        a.out[(long long)c * a.out_pitch] = (uint8_t)p0;
+      } else {
+        p0 = a.tokens[(long long)c * a.n_steps];
+      }
+    }
+    prev[n] = (p0 >= 0 && p0 < V) ? p0 : 0;
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int nsteps = *nsteps_sh;
+
+  if (warp == 0) {
+    // ============================== producer ==============================
+    if (lane == 0 && nsteps > 0) {
+      const uint64_t pol = tc::policy_evict_last();
+      long long it = 0;
+      bool ok = true;
+      for (int s = 0; s < nsteps && ok; ++s) {
+        for (int t = 0; t < a.tiles_per_step; ++t, ++it) {
+          const int st = (int)(it % kStages);
+          const uint32_t round = (uint32_t)(it / kStages);
+          if (!tc::mbar_wait(&empty[st], (round & 1u) ^ 1u, abort_flag, kWaitBudget)) { ok = false; break; }
+          tc::mbar_arrive_expect_tx(&full[st], kTileBytes);
+          tc::bulk_g2s(ring + st * kTileBytes, a.wtiles + (long long)t * kTileBytes, kTileBytes, &full[st], pol);
+        }
+      }
+      // every issued copy must land before the CTA may exit
+      for (long long j = *cons_sh; j < it; ++j) {
+        const int st = (int)(j % kStages);
+        const uint32_t round = (uint32_t)(j / kStages);
+        const long long t0 = clock64();
+        while (!tc::mbar_try_wait(&full[st], round & 1u)) {
+          if (clock64() - t0 > kWaitBudget) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ============================= MMA issuer =============================
+    if (lane == 0 && nsteps > 0) {
+      const uint32_t id = tc::idesc<KIND>(128, CT);
+      const uint32_t bbase = tc::smem_u32(bbuf);
+      const uint32_t rbase = tc::smem_u32(ring);
+      long long it = 0;
+      uint32_t act_phase = 0;
+      bool ok = true;
+      // D[col0 + mt*CT ...] = sum over ks of A(mt, ks) * B(ks)^T
+      auto gemm = [&](int n_mt, int n_ks, int col0) -> bool {
+        for (int mt = 0; mt < n_mt; ++mt) {
+          for (int ks = 0; ks < n_ks; ++ks, ++it) {
+            const int st = (int)(it % kStages);
+            const uint32_t round = (uint32_t)(it / kStages);
+            if (!tc::mbar_wait(&full[st], round & 1u, abort_flag, kWaitBudget)) return false;
+            tc::tc_fence_after();
+            const uint32_t a0 = rbase + st * kTileBytes;
+            const uint32_t b0 = bbase + ks * CT * 128;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              tc::mma<KIND>(tmem + (uint32_t)(col0 + mt * CT), tc::sdesc_sw128(a0 + kk * 32),
+                            tc::sdesc_sw128(b0 + kk * 32), id, (ks > 0 || kk > 0) ? 1u : 0u);
+            tc::mma_commit(&empty[st]);
+            *cons_sh = (int)(it + 1);
+          }
+        }
+        return true;
+      };
+      auto step_gemm = [&](int n_mt, int n_ks, int col0) -> bool {
+        if (!tc::mbar_wait(act_bar, act_phase, abort_flag, kWaitBudget)) return false;
+        act_phase ^= 1u;
+        tc::tc_fence_after();
+        if (!gemm(n_mt, n_ks, col0)) return false;
+        tc::mma_commit(mma_bar);
+        return true;
+      };
+      for (int s = 0; s < nsteps && ok; ++s) {
+        for (int l = 0; l < L && ok; ++l) {
+          ok = step_gemm(2 * MT_E, kD, 0)          // in_proj -> x | z
+               && step_gemm(1, kE, COL_XP)         // x_proj
+               && step_gemm(MT_E, 1, COL_DT)       // dt_proj
+               && step_gemm(MT_D, kE, 0)           // out_proj
+               && step_gemm(MT_F, kD, 0)           // ff.0
+               && step_gemm(MT_D, kF, 0);          // ff.2
+        }
+        ok = ok && step_gemm(MT_D, kD, 0)          // head.0
+             && step_gemm(2, kD, 0);               // head.2
+      }
+      // every issued MMA must retire before TMEM is released
+      tc::mma_commit(drain_bar);
+      const long long t0 = clock64();
+      while (!tc::mbar_try_wait(drain_bar, 0)) {
+        if (clock64() - t0 > kWaitBudget) break;
+      }
+    }
+  } else {
+    // ============================ compute warps ============================
+    const int ct = tid - 64;                 // 0..511
+    const int cw = ct >> 5;                  // compute warp 0..15
+    const int q = warp & 3;                  // TMEM lane quarter this warp may access
+    const int g = cw >> 2;                   // group 0..3 (covers all four quarters)
+    const int row = 32 * q + lane;           // row inside a 128-row M tile
+    const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
+    uint32_t mma_phase = 0;
+    RcEnc* encs = reinterpret_cast<RcEnc*>(smem + S::o_enc);
+    RcDec* decs = reinterpret_cast<RcDec*>(smem + S::o_enc);
+
+    auto arrive_act = [&]() {
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(act_bar);
+    };
+    // Wait for the GEMM just issued; the verdict is uniform over the 512 threads.
+    auto wait_mma = [&]() -> bool {
+      tc::mbar_wait(mma_bar, mma_phase, abort_flag, kWaitBudget);
+      mma_phase ^= 1u;
+      cbar_sync();
+      tc::tc_fence_after();
+      return *abort_flag == 0;
+    };
+    auto is_active = [&](int n, int t) -> bool {
+      const int c = c0 + n;
+      if (c >= a.n_chunks) return false;
+      if (mode == MODE_LOGITS) return true;
+      return t < a.lens[c];
+    };
+    // LayerNorm (eps 1e-5, biased variance, two passes) of CT rows of `src`
+    // (fp32 [CT][D]) into the B operand; a warp per chunk.
+    auto layernorm_to_b = [&](const float* src, const float* w, const float* b) {
+      constexpr int PL = D / 32;
+      for (int n = cw; n < CT; n += 16) {
+        float v[PL];
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) { v[i] = src[n * D + lane + 32 * i]; s += v[i]; }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float mean = s * (1.0f / D);
+        float var = 0.f;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) { const float dl = v[i] - mean; var += dl * dl; }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+        const float rstd = rsqrtf(var * (1.0f / D) + 1e-5f);
+#pragma unroll
+        for (int i = 0; i < PL; ++i) {
+          const int f = lane + 32 * i;
+          tc::store_operand<KIND>(bbuf, n, f, CT, (v[i] - mean) * rstd * __ldg(w + f) + __ldg(b + f));
+        }
+      }
+    };
+
+    bool ok = true;
+    for (int s = 0; s < nsteps && ok; ++s) {
+      const int t = (mode == MODE_LOGITS) ? s : s + 1;     // position predicted / coded
+      const bool load_state = !(a.fresh && s == 0);
+      // ---- embedding
+      for (int i = ct; i < CT * D; i += kComputeThreads) {
+        const int n = i / D, f = i - (i / D) * D;
+        hres[i] = __ldg(P + o_emb + (long long)prev[n] * D + f);
+      }
+      cbar_sync();
+      for (int l = 0; l < L && ok; ++l) {
+        const float* lp = P + (long long)LP::stride * l;
+        // ---- LN1 -> B ; in_proj
+        layernorm_to_b(hres, lp + LP::ln1w, lp + LP::ln1b);
+        arrive_act();
+        if (!(ok = wait_mma())) break;
+        // ---- causal conv (width 4) + SiLU, thread per channel; xc -> B and TMEM
+        for (int mt = g; mt < MT_E; mt += 4) {
+          const int e = mt * 128 + row;
+          float xv[16];
+          tc::tmem_ld16(tq + (uint32_t)(COL_X + mt * CT), xv);
+          const float4 w = __ldg(reinterpret_cast<const float4*>(lp + LP::convw) + e);
+          const float cb = __ldg(lp + LP::convb + e);
+#pragma unroll 4
+          for (int n = 0; n < CT; ++n) {
+            const bool act = is_active(n, t);
+            const long long si = ((long long)(c0 + n) * L + l) * E + e;
+            float4 st = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (act && load_state) st = a.conv_state[si];
+            float acc = cb;
+            acc = fmaf(w.x, st.x, acc);
+            acc = fmaf(w.y, st.y, acc);
+            acc = fmaf(w.z, st.z, acc);
+            acc = fmaf(w.w, xv[n], acc);
+            const float xc = silu_f(acc);
+            if (act) a.conv_state[si] = make_float4(st.y, st.z, xv[n], 0.f);
+            tc::store_operand<KIND>(bbuf, n, e, CT, xc);
+            xv[n] = xc;
+          }
+          tc::tmem_st16(tq + (uint32_t)(COL_X + mt * CT), xv);
+        }
+        arrive_act();
+        if (!(ok = wait_mma())) break;
+        // ---- x_proj epilogue: dt_r -> B (K slice 0, zero padded), B/C -> smem
+        if (g == 0) {
+          float v[16];
+          tc::tmem_ld16(tq + (uint32_t)COL_XP, v);
+          if (row < DBC) {
+#pragma unroll
+            for (int n = 0; n < CT; ++n) dbc[n * 64 + row] = v[n];
+          }
+          if (row < PER) {
+#pragma unroll
+            for (int n = 0; n < CT; ++n) tc::store_operand<KIND>(bbuf, n, row, CT, row < R ? v[n] : 0.f);
+          }
+        }
+        arrive_act();
+        if (!(ok = wait_mma())) break;
+        // ---- selective scan + D skip + SiLU(z) gate, thread per channel
+        for (int mt = g; mt < MT_E; mt += 4) {
+          const int e = mt * 128 + row;
+          float xc[16], z[16], dtr[16];
+          tc::tmem_ld16(tq + (uint32_t)(COL_X + mt * CT), xc);
+          tc::tmem_ld16(tq + (uint32_t)(COL_Z + mt * CT), z);
+          tc::tmem_ld16(tq + (uint32_t)(COL_DT + mt * CT), dtr);
+          float A2[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 t4 = __ldg(reinterpret_cast<const float4*>(lp + LP::A2) + e * 4 + j);
+            A2[4 * j] = t4.x; A2[4 * j + 1] = t4.y; A2[4 * j + 2] = t4.z; A2[4 * j + 3] = t4.w;
+          }
+          const float Dp = __ldg(lp + LP::Dp + e);
+          const float bdt = __ldg(lp + LP::dtb + e);
+          for (int n = 0; n < CT; ++n) {
+            const bool act = is_active(n, t);
+            const long long si = (((long long)(c0 + n) * L + l) * E + e) * 4;
+            float h[16];
+            if (act && load_state) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float4 t4 = a.ssm_state[si + j];
+                h[4 * j] = t4.x; h[4 * j + 1] = t4.y; h[4 * j + 2] = t4.z; h[4 * j + 3] = t4.w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) h[j] = 0.f;
+            }
+            const float dtv = softplus_f(dtr[n] + bdt);
+            const float dx = dtv * xc[n];
+            const float* bc = dbc + n * 64 + R;
+            float y = 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              h[j] = fmaf(h[j], exp2f(dtv * A2[j]), dx * bc[j]);
+              y = fmaf(h[j], bc[16 + j], y);
+            }
+            if (act) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                a.ssm_state[si + j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+            }
+            y = fmaf(Dp, xc[n], y);
+            y *= silu_f(z[n]);
+            tc::store_operand<KIND>(bbuf, n, e, CT, y);
+          }
+        }
+        arrive_act();
+        if (!(ok = wait_mma())) break;
+        // ---- out_proj epilogue -> scratch, then LN2 -> B
+        if (g < MT_D) {
+          float v[16];
+          tc::tmem_ld16(tq + (uint32_t)(g * CT), v);
+          const int f = g * 128 + row;
+          if (f < D) {
+#pragma unroll
+            for (int n = 0; n < CT; ++n) scr[n * D + f] = v[n];
+          }
+        }
+        cbar_sync();
+        layernorm_to_b(scr, lp + LP::ln2w, lp + LP::ln2b);
+        arrive_act();
+        if (!(ok = wait_mma())) break;
+        // ---- ff.0 epilogue: + b1, exact GELU -> B
+        for (int mt = g; mt < MT_F; mt += 4) {
+          float v[16];
+          tc::tmem_ld16(tq + (uint32_t)(mt * CT), v);
+          const int f = mt * 128 + row;
+          const float b = __ldg(lp + LP::b1 + f);
+#pragma unroll
+          for (int n = 0; n < CT; ++n) tc::store_operand<KIND>(bbuf, n, f, CT, gelu_f(v[n] + b));
+        }
+        arrive_act();
+        if (!(ok = wait_mma())) break;
+        // ---- ff.2 epilogue: residual update
+        if (g < MT_D) {
+          float v[16];
+          tc::tmem_ld16(tq + (uint32_t)(g * CT), v);
+          const int f = g * 128 + row;
+          if (f < D) {
+            const float b = __ldg(lp + LP::b2 + f);
+#pragma unroll
+            for (int n = 0; n < CT; ++n) hres[n * D + f] += v[n] + b;
+          }
+        }
+        cbar_sync();
+      }
+      if (!ok) break;
+      // ---- head.0: Linear + ReLU
+      for (int i = ct; i < CT * D; i += kComputeThreads) {
+        const int n = i / D, f = i - (i / D) * D;
+        tc::store_operand<KIND>(bbuf, n, f, CT, hres[i]);
+      }
+      arrive_act();
+      if (!(ok = wait_mma())) break;
+      if (g < MT_D) {
+        float v[16];
+        tc::tmem_ld16(tq + (uint32_t)(g * CT), v);
+        const int f = g * 128 + row;
+        if (f < D) {
+          const float b = __ldg(P + o_bh0 + f);
+#pragma unroll
+          for (int n = 0; n < CT; ++n) tc::store_operand<KIND>(bbuf, n, f, CT, fmaxf(v[n] + b, 0.f));
+        }
+      }
+      arrive_act();
+      if (!(ok = wait_mma())) break;
+      // ---- head.2: logits -> scratch
+      if (g < 2) {
+        float v[16];
+        tc::tmem_ld16(tq + (uint32_t)(g * CT), v);
+        const int vv = g * 128 + row;
+        const float b = __ldg(P + o_bh2 + vv);
+#pragma unroll
+        for (int n = 0; n < CT; ++n) scr[n * 256 + vv] = v[n] + b;
+      }
+      cbar_sync();
+      // ---- quantiser + range coder, a warp per chunk
+      for (int n = cw; n < CT; n += 16) {
+        const int c = c0 + n;
+        if (!is_active(n, t)) continue;
+        if (mode == MODE_LOGITS) {
+          float* dst = a.logits + ((long long)c * a.n_steps + s) * V;
+          for (int v = lane; v < V; v += 32) dst[v] = scr[n * 256 + v];
+          if (lane == 0) {
+            const int nx = (s + 1 < a.n_steps) ? a.tokens[(long long)c * a.n_steps + s + 1] : 0;
+            prev[n] = (nx >= 0 && nx < V) ? nx : 0;
+          }
+          continue;
+        }
+        float lv[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) lv[k] = scr[n * 256 + lane * 8 + k];
+        uint32_t fr[8], base;
+        bq_quantise_warp<8>(lv, V, a.precision, lane, fr, base);
+        if (mode == MODE_ENCODE) {
+          int sym = a.bytes[(long long)c * a.in_pitch + t];
+          if (sym >= V) {
+            if (lane == 0) atomicOr(a.err, RC_ERR_SYMBOL);
+            sym = 0;
+          }
+          uint32_t left, freq;
+          bq_lookup_warp<8>(fr, base, sym, lane, left, freq);
+          if (lane == 0) {
+            RcEnc st = encs[n];
+            rc_enc_put(st, left, freq, a.precision, a.words + (long long)c * a.pitch_words, a.pitch_words, a.err);
+            encs[n] = st;
+            prev[n] = sym;
+          }
+        } else {
+          RcDec st = decs[n];
+          unsigned long long scale;
+          const uint32_t target = rc_dec_target(st, a.precision, scale);
+          uint32_t left, freq;
+          const int sym = bq_search_warp<8>(fr, base, target, lane, left, freq);
+          if (lane == 0) {
+            int nw = a.sizes_in[c];
+            nw = nw < 0 ? 0 : (nw > a.pitch_words ? a.pitch_words : nw);
+            rc_dec_advance(st, scale, left, freq, a.words_in + (long long)c * a.pitch_words, nw);
+            decs[n] = st;
+            a.out[(long long)c * a.out_pitch + t] = (uint8_t)sym;
+            prev[n] = sym;
+          }
+        }
+      }
+      cbar_sync();
+    }
+    if (ok && mode == MODE_ENCODE && ct < CT) {
+      const int c = c0 + ct;
+      if (c < a.n_chunks) {
+        RcEnc st = encs[ct];
+        a.sizes[c] = rc_enc_finish(st, a.words + (long long)c * a.pitch_words, a.pitch_words, a.err);
+      }
+    }
+  }
+
+  // ------------------------------ teardown ------------------------------
+  tc::tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && *abort_flag) atomicOr(a.err, RC_ERR_TIMEOUT);
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Diagnostic single-CTA GEMM through the same pipeline pieces:
+//   out[m][n] = sum_k W[m][k] * X[n][k]   (W pre-packed tiles, X via store_operand)
+// ---------------------------------------------------------------------------
+template <int KIND>
+__global__ void __launch_bounds__(256, 1) k_diag_gemm(const uint8_t* wtiles, const float* X, float* out, int M, int K,
+                                                      uint32_t* err) {
+  constexpr int CT = kCT;
+  constexpr int PER = 128 / tc::OpKind<KIND>::kElemBytes;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tile = smem;                              // one A tile
+  uint8_t* bbuf = smem + kTileBytes;                 // B operand, K up to 1024 fp32
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTileBytes + CT * 4096);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 5);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_mt = M / 128, n_ks = K / PER;
+  if (tid == 0) {
+    tc::mbar_init(&bars[0], 1);   // tile landed
+    tc::mbar_init(&bars[1], 1);   // MMAs done
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) { tc::tmem_alloc(tslot, 512); tc::tmem_relinquish(); }
+  for (int i = tid; i < CT * K; i += blockDim.x) tc::store_operand<KIND>(bbuf, i / K, i % K, CT, X[i]);
+  tc::fence_proxy_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tslot;
+  uint32_t ph = 0;
+  for (int mt = 0; mt < n_mt; ++mt) {
+    for (int ks = 0; ks < n_ks; ++ks) {
+      if (tid == 0) {
+        tc::mbar_arrive_expect_tx(&bars[0], kTileBytes);
+        tc::bulk_g2s(tile, wtiles + ((long long)mt * n_ks + ks) * kTileBytes, kTileBytes, &bars[0],
+                     tc::policy_evict_first());
+        if (tc::mbar_wait(&bars[0], ph, abort_flag, kWaitBudget)) {
+          tc::tc_fence_after();
+          const uint32_t a0 = tc::smem_u32(tile), b0 = tc::smem_u32(bbuf) + ks * CT * 128;
+          for (int kk = 0; kk < 4; ++kk)
+            tc::mma<KIND>(tmem + (uint32_t)(mt * CT), tc::sdesc_sw128(a0 + kk * 32), tc::sdesc_sw128(b0 + kk * 32),
+                          tc::idesc<KIND>(128, CT), (ks > 0 || kk > 0) ? 1u : 0u);
+          tc::mma_commit(&bars[1]);
+          tc::mbar_wait(&bars[1], ph, abort_flag, kWaitBudget);   // tile buffer reusable
+        }
+      }
+      ph ^= 1u;
+      __syncthreads();
+    }
+  }
+  tc::tc_fence_after();
+  if (warp < 4) {
+    for (int mt = 0; mt < n_mt; ++mt) {
+      float v[16];
+      tc::tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(mt * CT), v);
+      const int m = mt * 128 + 32 * warp + lane;
+      for (int n = 0; n < CT; ++n) out[(long long)m * CT + n] = v[n];
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && *abort_flag) atomicOr(err, RC_ERR_TIMEOUT);
+  if (warp == 1) { tc::tc_fence_after(); tc::tmem_dealloc(tmem, 512); }
+}
+
+// ------------------------------- host side ---------------------------------
+static uint32_t f32_bits(float f) { uint32_t u; std::memcpy(&u, &f, 4); return u; }
+
+// Round-to-nearest (ties away) to tf32, as cvt.rna.tf32.f32 does.
+static uint32_t to_tf32_bits(float f) {
+  uint32_t u = f32_bits(f);
+  if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
+  return u;
+}
+
+// Append the SW128 tile images of W [M_real x K] (row-major fp32; rows >= M_real
+// and columns >= K_real are zero) as n_mt x n_ks tiles, mt outer.
+static void pack_tiles(std::vector<uint8_t>& out, const float* W, int M_real, int K_real, int ldw, int n_mt,
+                       int n_ks, int kind) {
+  const int eb = kind == 0 ? 4 : 2;
+  const int per = 128 / eb;
+  for (int mt = 0; mt < n_mt; ++mt) {
+    for (int ks = 0; ks < n_ks; ++ks) {
+      const size_t base = out.size();
+      out.resize(base + kTileBytes, 0);
+      uint8_t* t = out.data() + base;
+      for (int r = 0; r < 128; ++r) {
+        const int m = mt * 128 + r;
+        for (int e = 0; e < per; ++e) {
+          const int k = ks * per + e;
+          const float v = (m < M_real && k < K_real) ? W[(size_t)m * ldw + k] : 0.0f;
+          const int byte = e * eb;
+          const int chunk = byte >> 4;
+          uint8_t* p = t + r * 128 + (((chunk ^ (r & 7)) << 4) | (byte & 15));
+          if (kind == 0) {
+            const uint32_t b = to_tf32_bits(v);
+            std::memcpy(p, &b, 4);
+          } else if (kind == 1) {
+            const unsigned short h = __half_as_ushort(__float2half_rn(v));
+            std::memcpy(p, &h, 2);
+          } else {
+            const unsigned short h = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+            std::memcpy(p, &h, 2);
+          }
+        }
+      }
+    }
+  }
+}
+
+}  // namespace boa
+
+using namespace boa;
+
+struct boa_model {
+  int D, L, V, kind, device;
+  TilePlan plan;
+  uint8_t* d_tiles = nullptr;
+  float* d_params = nullptr;
+  uint32_t* d_err = nullptr;
+  size_t params_floats = 0;
+};
+
+namespace {
+
+// Walk the flat convert_boa_weights.py order (convert_boa_weights.py:16-135).
+struct FlatReader {
+  const float* p;
+  size_t n, pos = 0;
+  bool ok = true;
+  const float* take(size_t k) {
+    if (pos + k > n) { ok = false; return nullptr; }
+    const float* r = p + pos;
+    pos += k;
+    return r;
+  }
+};
+
+template <int D>
+int build_model(boa_model* m, const float* flat, size_t n_floats, std::vector<uint8_t>& tiles,
+                std::vector<float>& params) {
+  using LP = LayerParams<D>;
+  const int E = 2 * D, R = cdiv(D, 16), DBC = R + 32, F = 4 * D, V = m->V, L = m->L, kind = m->kind;
+  const TilePlan& p = m->plan;
+  FlatReader fr{flat, n_floats};
+  const float* emb = fr.take((size_t)V * D);
+  params.assign((size_t)LP::stride * L + D + 256 + (size_t)V * D, 0.0f);
+  for (int l = 0; l < L; ++l) {
+    float* lp = params.data() + (size_t)LP::stride * l;
+    const float* ln1w = fr.take(D); const float* ln1b = fr.take(D);
+    const float* w_in = fr.take((size_t)2 * E * D); fr.take((size_t)2 * E);      // in_proj.bias slot (zeros)
+    const float* convw = fr.take((size_t)E * 4); const float* convb = fr.take(E);
+    const float* w_x = fr.take((size_t)DBC * E);
+    const float* w_dt = fr.take((size_t)E * R); const float* b_dt = fr.take(E);
+    const float* A_log = fr.take((size_t)E * 16); const float* Dv = fr.take(E);
+    const float* w_out = fr.take((size_t)D * E); fr.take(D);                     // out_proj.bias slot (zeros)
+    const float* ln2w = fr.take(D); const float* ln2b = fr.take(D);
+    const float* w1 = fr.take((size_t)F * D); const float* b1 = fr.take(F);
+    const float* w2 = fr.take((size_t)D * F); const float* b2 = fr.take(D);
+    if (!fr.ok) return boa_fail(BOA_ERR_ARG, "boa_model_create: flat weight vector too short for the config");
+    std::memcpy(lp + LP::ln1w, ln1w, D * 4); std::memcpy(lp + LP::ln1b, ln1b, D * 4);
+    std::memcpy(lp + LP::convw, convw, (size_t)E * 16); std::memcpy(lp + LP::convb, convb, E * 4);
+    std::memcpy(lp + LP::dtb, b_dt, E * 4); std::memcpy(lp + LP::Dp, Dv, E * 4);
+    for (int i = 0; i < E * 16; ++i)   // A*log2(e) with A = -exp(A_log), for exp2 in the scan
+      lp[LP::A2 + i] = (float)(-std::exp((double)A_log[i]) * 1.4426950408889634);
+    std::memcpy(lp + LP::ln2w, ln2w, D * 4); std::memcpy(lp + LP::ln2b, ln2b, D * 4);
+    std::memcpy(lp + LP::b1, b1, F * 4); std::memcpy(lp + LP::b2, b2, D * 4);
+    pack_tiles(tiles, w_in, 2 * E, D, D, 2 * p.mtE, p.kD, kind);
+    pack_tiles(tiles, w_x, DBC, E, E, 1, p.kE, kind);
+    pack_tiles(tiles, w_dt, E, R, R, p.mtE, 1, kind);
+    pack_tiles(tiles, w_out, D, E, E, p.mtD, p.kE, kind);
+    pack_tiles(tiles, w1, F, D, D, p.mtF, p.kD, kind);
+    pack_tiles(tiles, w2, D, F, F, p.mtD, p.kF, kind);
+  }
+  const float* wh0 = fr.take((size_t)D * D); const float* bh0 = fr.take(D);
+  const float* wh2 = fr.take((size_t)V * D); const float* bh2 = fr.take(V);
+  if (!fr.ok) return boa_fail(BOA_ERR_ARG, "boa_model_create: flat weight vector too short for the config");
+  if (fr.pos != n_floats) return boa_fail(BOA_ERR_ARG, "boa_model_create: flat weight vector longer than the config");
+  float* g = params.data() + (size_t)LP::stride * L;
+  std::memcpy(g, bh0, D * 4);
+  std::memcpy(g + D, bh2, V * 4);
+  std::memcpy(g + D + 256, emb, (size_t)V * D * 4);
+  pack_tiles(tiles, wh0, D, D, D, p.mtD, p.kD, kind);
+  pack_tiles(tiles, wh2, V, D, D, 2, p.kD, kind);
+  if (tiles.size() != (size_t)p.per_step * kTileBytes)
+    return boa_fail(BOA_ERR_ARG, "boa_model_create: internal tile count mismatch");
+  return BOA_OK;
+}
+
+size_t conv_state_bytes(const boa_model* m, int n) { return (size_t)n * m->L * (2 * m->D) * 16; }
+size_t ssm_state_bytes(const boa_model* m, int n) { return (size_t)n * m->L * (2 * m->D) * 64; }
+
+template <int D, int KIND>
+int launch_step_t(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
+  const int smem = Smem<D, KIND>::ALLOC;
+  BOA_CUDA(cudaFuncSetAttribute(k_boa_step<D, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int grid = cdiv(n_chunks, kCT);
+  k_boa_step<D, KIND><<<grid, kThreads, smem, s>>>(a);
+  BOA_CUDA(cudaGetLastError());
+  return BOA_OK;
+}
+
+int launch_step(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
+  a.n_layers = m->L;
+  a.vocab = m->V;
+  a.tiles_per_step = m->plan.per_step;
+  a.wtiles = m->d_tiles;
+  a.params = m->d_params;
+  a.err = m->d_err;
+#define BOA_DISPATCH(DD)                                            \
+  if (m->D == DD) {                                                 \
+    if (m->kind == 0) return launch_step_t<DD, 0>(m, a, n_chunks, s); \
+    if (m->kind == 1) return launch_step_t<DD, 1>(m, a, n_chunks, s); \
+    return launch_step_t<DD, 2>(m, a, n_chunks, s);                 \
+  }
+  BOA_DISPATCH(64)
+  BOA_DISPATCH(256)
+  BOA_DISPATCH(512)
+#undef BOA_DISPATCH
+  return boa_fail(BOA_ERR_UNSUPPORTED, "d_model must be 64, 256 or 512");
+}
+
+int check_err(const boa_model* m, cudaStream_t s) {
+  uint32_t e = 0;
+  BOA_CUDA(cudaMemcpyAsync(&e, m->d_err, 4, cudaMemcpyDeviceToHost, s));
+  BOA_CUDA(cudaStreamSynchronize(s));
+  if (e) {
+    cudaMemsetAsync(m->d_err, 0, 4, s);
+    if (e & RC_ERR_TIMEOUT) return boa_fail(BOA_ERR_TIMEOUT, "model kernel: a bounded device wait timed out");
+    if (e & RC_ERR_OVERFLOW) return boa_fail(BOA_ERR_OVERFLOW, "codec: a compressed stream exceeded its pitch");
+    if (e & RC_ERR_SYMBOL) return boa_fail(BOA_ERR_ARG, "codec: symbol outside the vocabulary");
+  }
+  return BOA_OK;
+}
+
+int workspace_split(const boa_model* m, int n, void* ws, size_t ws_bytes, float4** conv, float4** ssm) {
+  const size_t need = boa_model_workspace_bytes(m, n);
+  if (!ws || ws_bytes < need) return boa_fail(BOA_ERR_ARG, "workspace too small (see boa_model_workspace_bytes)");
+  if (reinterpret_cast<uintptr_t>(ws) % 16) return boa_fail(BOA_ERR_ARG, "workspace must be 16-byte aligned");
+  *ssm = reinterpret_cast<float4*>(ws);
+  *conv = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(ws) + ssm_state_bytes(m, n));
+  return BOA_OK;
+}
+
+}  // namespace
 
 extern "C" {
-BOA_API int boa_model_create(boa_model** out, int, int, int, const float*, size_t, int, int) {
-  if (out) *out = nullptr;
-  return boa_fail(BOA_ERR_UNSUPPORTED, "boa_model_create: not built yet");
+
+BOA_API int boa_model_create(boa_model** out, int d_model, int n_layers, int vocab, const float* host_flat_weights,
+                             size_t n_floats, int weight_format, int device) {
+  if (!out) return boa_fail(BOA_ERR_ARG, "boa_model_create: null out");
+  *out = nullptr;
+  if (d_model != 64 && d_model != 256 && d_model != 512)
+    return boa_fail(BOA_ERR_UNSUPPORTED, "boa_model_create: d_model must be 64, 256 or 512");
+  if (n_layers < 1 || n_layers > 64) return boa_fail(BOA_ERR_ARG, "boa_model_create: n_layers must be in [1, 64]");
+  if (vocab < 2 || vocab > 256) return boa_fail(BOA_ERR_ARG, "boa_model_create: vocab must be in [2, 256]");
+  if (weight_format < 0 || weight_format > 2) return boa_fail(BOA_ERR_ARG, "boa_model_create: unknown weight format");
+  if (!host_flat_weights) return boa_fail(BOA_ERR_ARG, "boa_model_create: null weights");
+  if (d_model == 512 && weight_format == BOA_WEIGHTS_TF32)
+    return boa_fail(BOA_ERR_UNSUPPORTED, "boa_model_create: d_model 512 needs 16-bit weights (bf16 or fp16)");
+  BOA_CUDA(cudaSetDevice(device));
+  boa_model* m = new boa_model();
+  m->D = d_model; m->L = n_layers; m->V = vocab; m->kind = weight_format; m->device = device;
+  m->plan = make_plan(d_model, n_layers, weight_format);
+  std::vector<uint8_t> tiles;
+  std::vector<float> params;
+  int rc = BOA_ERR_UNSUPPORTED;
+  if (d_model == 64) rc = build_model<64>(m, host_flat_weights, n_floats, tiles, params);
+  if (d_model == 256) rc = build_model<256>(m, host_flat_weights, n_floats, tiles, params);
+  if (d_model == 512) rc = build_model<512>(m, host_flat_weights, n_floats, tiles, params);
+  if (rc != BOA_OK) { delete m; return rc; }
+  m->params_floats = params.size();
+  cudaError_t e = cudaMalloc(&m->d_tiles, tiles.size());
+  if (e == cudaSuccess) e = cudaMalloc(&m->d_params, params.size() * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->d_err, 4);
+  if (e == cudaSuccess) e = cudaMemcpy(m->d_tiles, tiles.data(), tiles.size(), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(m->d_params, params.data(), params.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(m->d_err, 0, 4);
+  if (e != cudaSuccess) {
+    boa_model_destroy(m);
+    return boa_fail(BOA_ERR_CUDA, std::string("boa_model_create: ") + cudaGetErrorString(e));
+  }
+  *out = m;
+  return BOA_OK;
 }
-BOA_API int boa_model_destroy(boa_model*) { return BOA_OK; }
-BOA_API size_t boa_model_workspace_bytes(const boa_model*, int) { return 0; }
-BOA_API int boa_model_step(boa_model*, int, const int32_t*, float*, void*, size_t, void*) {
-  return boa_fail(BOA_ERR_UNSUPPORTED, "boa_model_step: not built yet");
+
+BOA_API int boa_model_destroy(boa_model* m) {
+  if (!m) return BOA_OK;
+  cudaSetDevice(m->device);
+  cudaFree(m->d_tiles); cudaFree(m->d_params); cudaFree(m->d_err);
+  delete m;
+  return BOA_OK;
 }
-BOA_API int boa_model_logits(boa_model*, int, int, const int32_t*, float*, void*, size_t, void*) {
-  return boa_fail(BOA_ERR_UNSUPPORTED, "boa_model_logits: not built yet");
+
+BOA_API size_t boa_model_workspace_bytes(const boa_model* m, int n_chunks) {
+  if (!m || n_chunks < 1) return 0;
+  // state is addressed per CTA tile of 16 chunks, so round the count up
+  const int n = cdiv(n_chunks, kCT) * kCT;
+  return conv_state_bytes(m, n) + ssm_state_bytes(m, n);
 }
-BOA_API int boa_codec_encode(boa_model*, int, const uint8_t*, int64_t, const int32_t*, uint32_t*, int, int32_t*,
-                             int, void*, size_t, void*) {
-  return boa_fail(BOA_ERR_UNSUPPORTED, "boa_codec_encode: not built yet");
+
+BOA_API int boa_model_info(const boa_model* m, int* d_model, int* n_layers, int* vocab, int* weight_format,
+                           size_t* tile_bytes_per_step) {
+  if (!m) return boa_fail(BOA_ERR_ARG, "boa_model_info: null handle");
+  if (d_model) *d_model = m->D;
+  if (n_layers) *n_layers = m->L;
+  if (vocab) *vocab = m->V;
+  if (weight_format) *weight_format = m->kind;
+  if (tile_bytes_per_step) *tile_bytes_per_step = (size_t)m->plan.per_step * kTileBytes;
+  return BOA_OK;
 }
-BOA_API int boa_codec_decode(boa_model*, int, const uint32_t*, int, const int32_t*, const int32_t*, const uint8_t*,
-                             uint8_t*, int64_t, int, void*, size_t, void*) {
-  return boa_fail(BOA_ERR_UNSUPPORTED, "boa_codec_decode: not built yet");
+
+BOA_API int boa_model_logits(boa_model* m, int n, int n_steps, const int32_t* d_tokens, float* d_logits,
+                             void* d_workspace, size_t workspace_bytes, void* stream) {
+  if (!m || !d_tokens || !d_logits || n < 1 || n_steps < 1) return boa_fail(BOA_ERR_ARG, "boa_model_logits: bad argument");
+  BOA_CUDA(cudaSetDevice(m->device));
+  StepArgs a{};
+  int rc = workspace_split(m, n, d_workspace, workspace_bytes, &a.conv_state, &a.ssm_state);
+  if (rc) return rc;
+  a.mode = MODE_LOGITS; a.n_chunks = n; a.n_steps = n_steps; a.fresh = 1; a.precision = 16;
+  a.tokens = d_tokens; a.logits = d_logits;
+  cudaStream_t s = (cudaStream_t)stream;
+  rc = launch_step(m, a, n, s);
+  if (rc) return rc;
+  return check_err(m, s);
 }
+
+BOA_API int boa_model_step(boa_model* m, int n, const int32_t* d_tokens, float* d_logits, void* d_workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (!m || !d_tokens || !d_logits || n < 1) return boa_fail(BOA_ERR_ARG, "boa_model_step: bad argument");
+  BOA_CUDA(cudaSetDevice(m->device));
+  StepArgs a{};
+  int rc = workspace_split(m, n, d_workspace, workspace_bytes, &a.conv_state, &a.ssm_state);
+  if (rc) return rc;
+  a.mode = MODE_LOGITS; a.n_chunks = n; a.n_steps = 1; a.fresh = 0; a.precision = 16;
+  a.tokens = d_tokens; a.logits = d_logits;
+  cudaStream_t s = (cudaStream_t)stream;
+  rc = launch_step(m, a, n, s);
+  if (rc) return rc;
+  return check_err(m, s);
 }
+
+BOA_API int boa_codec_encode(boa_model* m, int n_chunks, const uint8_t* d_bytes, int64_t in_pitch,
+                             const int32_t* d_lens, uint32_t* d_words, int pitch_words, int32_t* d_sizes,
+                             int precision, void* d_workspace, size_t workspace_bytes, void* stream) {
+  if (!m || !d_bytes || !d_lens || !d_words || !d_sizes || n_chunks < 1 || pitch_words < 1)
+    return boa_fail(BOA_ERR_ARG, "boa_codec_encode: bad argument");
+  if (precision < 11 || precision > 24 || 2 * m->V > (1 << precision))
+    return boa_fail(BOA_ERR_ARG, "boa_codec_encode: precision out of range");
+  BOA_CUDA(cudaSetDevice(m->device));
+  StepArgs a{};
+  int rc = workspace_split(m, n_chunks, d_workspace, workspace_bytes, &a.conv_state, &a.ssm_state);
+  if (rc) return rc;
+  a.mode = MODE_ENCODE; a.n_chunks = n_chunks; a.fresh = 1; a.precision = precision;
+  a.bytes = d_bytes; a.in_pitch = in_pitch; a.lens = d_lens;
+  a.words = d_words; a.pitch_words = pitch_words; a.sizes = d_sizes;
+  cudaStream_t s = (cudaStream_t)stream;
+  rc = launch_step(m, a, n_chunks, s);
+  if (rc) return rc;
+  return check_err(m, s);
+}
+
+BOA_API int boa_codec_decode(boa_model* m, int n_chunks, const uint32_t* d_words, int pitch_words,
+                             const int32_t* d_sizes, const int32_t* d_lens, const uint8_t* d_first_bytes,
+                             uint8_t* d_out, int64_t out_pitch, int precision, void* d_workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (!m || !d_words || !d_sizes || !d_lens || !d_first_bytes || !d_out || n_chunks < 1 || pitch_words < 1)
+    return boa_fail(BOA_ERR_ARG, "boa_codec_decode: bad argument");
+  if (precision < 11 || precision > 24 || 2 * m->V > (1 << precision))
+    return boa_fail(BOA_ERR_ARG, "boa_codec_decode: precision out of range");
+  BOA_CUDA(cudaSetDevice(m->device));
+  StepArgs a{};
+  int rc = workspace_split(m, n_chunks, d_workspace, workspace_bytes, &a.conv_state, &a.ssm_state);
+  if (rc) return rc;
+  a.mode = MODE_DECODE; a.n_chunks = n_chunks; a.fresh = 1; a.precision = precision;
+  a.words_in = d_words; a.pitch_words = pitch_words; a.sizes_in = d_sizes; a.lens = d_lens;
+  a.first_bytes = d_first_bytes; a.out = d_out; a.out_pitch = out_pitch;
+  cudaStream_t s = (cudaStream_t)stream;
+  rc = launch_step(m, a, n_chunks, s);
+  if (rc) return rc;
+  return check_err(m, s);
+}
+
+BOA_API int boa_diag_gemm(int weight_format, int M, int K, const float* h_w, const float* h_x, float* h_out,
+                          int device) {
+  if (weight_format < 0 || weight_format > 2) return boa_fail(BOA_ERR_ARG, "boa_diag_gemm: bad format");
+  const int per = weight_format == 0 ? 32 : 64;
+  if (M < 128 || M % 128 || K < per || K % per || K > 1024 || M > 512)
+    return boa_fail(BOA_ERR_ARG, "boa_diag_gemm: M in {128..512} step 128, K multiple of the slice, <= 1024");
+  BOA_CUDA(cudaSetDevice(device));
+  std::vector<uint8_t> tiles;
+  pack_tiles(tiles, h_w, M, K, K, M / 128, K / per, weight_format);
+  uint8_t* d_t = nullptr; float *d_x = nullptr, *d_o = nullptr; uint32_t* d_e = nullptr;
+  cudaError_t e = cudaMalloc(&d_t, tiles.size());
+  if (e == cudaSuccess) e = cudaMalloc(&d_x, (size_t)kCT * K * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&d_o, (size_t)M * kCT * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&d_e, 4);
+  if (e == cudaSuccess) e = cudaMemcpy(d_t, tiles.data(), tiles.size(), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(d_x, h_x, (size_t)kCT * K * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(d_e, 0, 4);
+  const int smem = kTileBytes + kCT * 4096 + 64 + 1024;
+  if (e == cudaSuccess) {
+    if (weight_format == 0) {
+      cudaFuncSetAttribute(k_diag_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      k_diag_gemm<0><<<1, 256, smem>>>(d_t, d_x, d_o, M, K, d_e);
+    } else if (weight_format == 1) {
+      cudaFuncSetAttribute(k_diag_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      k_diag_gemm<1><<<1, 256, smem>>>(d_t, d_x, d_o, M, K, d_e);
+    } else {
+      cudaFuncSetAttribute(k_diag_gemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      k_diag_gemm<2><<<1, 256, smem>>>(d_t, d_x, d_o, M, K, d_e);
+    }
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  uint32_t err = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(h_out, d_o, (size_t)M * kCT * 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(&err, d_e, 4, cudaMemcpyDeviceToHost);
+  cudaFree(d_t); cudaFree(d_x); cudaFree(d_o); cudaFree(d_e);
+  if (e != cudaSuccess) return boa_fail(BOA_ERR_CUDA, std::string("boa_diag_gemm: ") + cudaGetErrorString(e));
+  if (err) return boa_fail(BOA_ERR_TIMEOUT, "boa_diag_gemm: bounded wait timed out");
+  return BOA_OK;
+}
+
+}  // extern "C"

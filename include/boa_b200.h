@@ -49,6 +49,7 @@ extern "C" {
 /* Projection weight formats for the model kernel. */
 #define BOA_WEIGHTS_TF32 0  /* fp32 weights, tf32 tensor-core products, fp32 accumulation */
 #define BOA_WEIGHTS_BF16 1  /* bf16 weights and activations, fp32 accumulation and state */
+#define BOA_WEIGHTS_F16 2   /* fp16 weights and activations (tf32-equal mantissa), fp32 accumulation and state */
 
 BOA_API const char* boa_last_error(void);
 BOA_API int boa_abi_version(void);
@@ -106,6 +107,9 @@ BOA_API int boa_model_create(boa_model** out, int d_model, int n_layers, int voc
                              const float* host_flat_weights, size_t n_floats, int weight_format,
                              int device);
 BOA_API int boa_model_destroy(boa_model* m);
+/* Shape of a built model and the projection-weight bytes streamed per byte step. */
+BOA_API int boa_model_info(const boa_model* m, int* d_model, int* n_layers, int* vocab, int* weight_format,
+                           size_t* tile_bytes_per_step);
 /* Bytes of device workspace (recurrent state + bookkeeping) that one
  * boa_codec_* / boa_model_logits call over n_chunks streams needs. */
 BOA_API size_t boa_model_workspace_bytes(const boa_model* m, int n_chunks);
@@ -141,6 +145,15 @@ BOA_API int boa_codec_decode(boa_model* m, int n_chunks, const uint32_t* d_words
                              const int32_t* d_sizes, const int32_t* d_lens, const uint8_t* d_first_bytes,
                              uint8_t* d_out, int64_t out_pitch, int precision, void* d_workspace,
                              size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Diagnostics (no reference counterpart).                                  */
+/* ------------------------------------------------------------------------ */
+/* One CTA of the model kernel's projection pipeline on host data:
+ * out[M][16] = W[M][K] . X[16][K]^T with W packed into the kernel's SW128 tiles
+ * (weight_format as for boa_model_create).  Synchronous; allocates scratch. */
+BOA_API int boa_diag_gemm(int weight_format, int M, int K, const float* h_w, const float* h_x, float* h_out,
+                          int device);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,76 @@
+"""The sm_100a model kernel vs the fp32 oracle (probabilities within 1e-3), its
+tensor-core pipeline vs fp64 products, and batch/grid invariance (bitwise)."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from boa_b200 import _native as _n
+from oracle import model_oracle as mo
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("fmt,tol", [(0, 2e-3), (1, 2e-3), (2, 1.6e-2)])
+@pytest.mark.parametrize("M,K", [(128, 64), (256, 256), (512, 1024)])
+def test_diag_gemm(fmt, tol, M, K):
+    rng = np.random.default_rng(M + K + fmt)
+    W = rng.normal(0, 1, (M, K)).astype(np.float32)
+    X = rng.normal(0, 1, (16, K)).astype(np.float32)
+    out = np.zeros((M, 16), np.float32)
+    _n.call("boa_diag_gemm", fmt, M, K, W.ctypes.data_as(ctypes.c_void_p), X.ctypes.data_as(ctypes.c_void_p),
+            out.ctypes.data_as(ctypes.c_void_p), 0)
+    ref = W.astype(np.float64) @ X.astype(np.float64).T
+    err = np.abs(out - ref).max() / np.sqrt(K)
+    assert err < tol, err
+
+
+def _native_logits(model, tokens):
+    x = torch.from_numpy(tokens).cuda()
+    return model(x).cpu()
+
+
+def _oracle_logits(model, tokens, dtype=torch.float64):
+    sd = {k: v.detach().cpu() for k, v in model.state_dict().items()}
+    cfg = mo.config_from_state_dict(sd)
+    return mo.forward(sd, cfg, torch.from_numpy(tokens).long(), dtype=dtype).float()
+
+
+@pytest.mark.parametrize("d,L,fmt", [(64, 2, "tf32"), (64, 2, "fp16"), (256, 2, "tf32"), (256, 2, "fp16"),
+                                     (512, 1, "bf16")])
+def test_logits_match_oracle(d, L, fmt):
+    from model import seeded_model
+    m = seeded_model(d, L, weight_format=fmt)
+    rng = np.random.default_rng(d + L)
+    toks = rng.integers(0, 256, (20, 48)).astype(np.int64)
+    got = _native_logits(m, toks)
+    ref = _oracle_logits(m, toks)
+    assert torch.isfinite(got).all()
+    pdiff = (torch.softmax(got, -1) - torch.softmax(ref, -1)).abs().max().item()
+    ldiff = (got - ref).abs().max().item()
+    print(f"d={d} L={L} {fmt}: max |dp| = {pdiff:.3e}, max |dlogit| = {ldiff:.3e}")
+    assert pdiff < 1e-3
+
+
+def test_batch_and_grid_invariance():
+    from model import seeded_model
+    m = seeded_model(64, 2)
+    rng = np.random.default_rng(3)
+    toks = rng.integers(0, 256, (37, 24)).astype(np.int64)
+    full = _native_logits(m, toks)
+    for idx in ([5], [0, 1, 2, 3, 4, 5, 6], list(range(36, -1, -3))):
+        sub = _native_logits(m, toks[idx])
+        assert torch.equal(sub, full[idx])
+
+
+def test_step_matches_forward():
+    from model import seeded_model
+    m = seeded_model(64, 2)
+    rng = np.random.default_rng(4)
+    toks = torch.from_numpy(rng.integers(0, 256, (9, 12))).cuda()
+    full = m(toks)
+    st = m.init_stream(max_len=12, batch_size=9, device="cuda")
+    for t in range(12):
+        lg = m.step(toks[:, t], st)
+        assert torch.equal(lg, full[:, t]), t
