@@ -1,0 +1,382 @@
+#!/usr/bin/env python
+"""Benchmark of the BoaConstrictor compress/decompress hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
+
+A step is one full pass of the hot path over one batch of synthetic input:
+compress every chunk of the configuration's input, then decompress it again
+(the round trip is verified on the first warm-up step).  Default workload is
+configuration 2 of the benchmark spec: 64 MiB of seeded HEP-like event
+records, chunks_count = 1000, BoaConstrictor d_model 256 / 8 layers, seeded
+random init.  With N ranks (torchrun, one GPU each) every rank codes its own
+1000-chunk shard of an N x 64 MiB job ("scaling": "weak"); the only
+collective is the all-reduce that gathers per-chunk lengths, outside the timed
+kernels.
+
+``value`` is the whole-job round-trip throughput with inputs resident in HBM:
+N x bytes / max over ranks of (compress + decompress) device time, in MiB/s
+(2^20 B/s, the unit the reference's C++ port prints, boa.cpp:39).  ``e2e`` is
+the same through the public host API (codec.compress_GPU / decompress_GPU:
+pinned host bytes in, host word lists out, and back).
+
+``--impl reference`` times the reference algorithm's CPU restatement
+(oracle/codec_oracle.py: fp32 model + softmax + the reference coder at
+PRECISION 24) on this host's cores over a bounded sample of the workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "boa-constrictor_b200"))
+
+MiB = 1 << 20
+
+CONFIGS = {
+    1: dict(name="config1 markov 1 MiB, chunks_count=16, d_model=64, num_layers=2", d=64, L=2, chunks=16,
+            data=("markov", 1 << 20), fmt="tf32"),
+    2: dict(name="config2 hep-records 64 MiB, chunks_count=1000, d_model=256, num_layers=8", d=256, L=8,
+            chunks=1000, data=("hep", 64 * MiB), fmt="tf32"),
+    3: dict(name="config3 hep-records 64 MiB, chunks_count=8192, d_model=256, num_layers=8", d=256, L=8,
+            chunks=8192, data=("hep", 64 * MiB), fmt="tf32"),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--weights", default=None, choices=["tf32", "fp16", "bf16"])
+    ap.add_argument("--size", type=int, default=None, help="override input bytes (testing)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def make_data(cfg, size=None):
+    from boa_b200 import synthetic
+    kind, n = cfg["data"]
+    n = size or n
+    return synthetic.markov(n, 1) if kind == "markov" else synthetic.hep_records(n, 2)
+
+
+def chunk_array(data: bytes, n_chunks: int):
+    import numpy as np
+    from boa_b200 import container as C
+    chunk_len, n, last = C.chunking(len(data), 0, n_chunks)
+    lens = [chunk_len] * (n - 1) + [last]
+    arr = np.zeros((n, chunk_len), dtype=np.uint8)
+    buf = np.frombuffer(data, dtype=np.uint8)
+    full = (n - 1) * chunk_len
+    arr[:n - 1] = buf[:full].reshape(n - 1, chunk_len)
+    arr[n - 1, :last] = buf[full:]
+    return arr, lens
+
+
+def state_bytes_per_coded_byte(d, L):
+    """Algorithmic HBM bytes per coded byte: read + write of the recurrent
+    state, SSM (L * E * 16 fp32) and conv window (L * E * 3 fp32)."""
+    E = 2 * d
+    return 2 * L * E * (16 + 3) * 4
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.remove(self.path)
+        except Exception:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for nm, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        loaded = [s for s in sm if s > 300] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return 6650.0, "fallback 6.65 TB/s"
+
+
+def traffic_per_coded_byte():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        return float(json.load(open(p))["k_boa_step"]["dram_bytes_per_coded_byte"])
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+def cpu_baseline(cfg, arr, lens, seconds_target=20.0):
+    """The reference algorithm's CPU restatement on a bounded sample."""
+    import numpy as np
+    import torch
+    from model import seeded_model
+    from oracle import codec_oracle as co
+    torch.set_num_threads(os.cpu_count() or 1)
+    sd = {k: v.float() for k, v in seeded_model(cfg["d"], cfg["L"]).state_dict().items()}
+    n_s = min(32, arr.shape[0])
+    L_s = 64
+    # calibrate the sample length so the run takes about seconds_target
+    chunks = [arr[i, :L_s] for i in range(n_s)]
+    t0 = time.perf_counter()
+    co.compress(sd, chunks)
+    dt = time.perf_counter() - t0
+    L_s = int(max(64, min(arr.shape[1], L_s * (seconds_target / 2) / max(dt, 1e-3))))
+    chunks = [arr[i, :L_s] for i in range(n_s)]
+    t0 = time.perf_counter()
+    comp, first, ls = co.compress(sd, chunks)
+    t1 = time.perf_counter()
+    out = co.decompress(sd, comp, ls, first)
+    t2 = time.perf_counter()
+    assert all(np.array_equal(a, b) for a, b in zip(out, chunks))
+    nbytes = n_s * L_s
+    return {"value": nbytes / MiB / (t2 - t0), "unit": "MiB/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n_s} chunks x first {L_s} bytes of the workload's chunks, compress + decompress",
+            "compress_MiBps": nbytes / MiB / (t1 - t0), "decompress_MiBps": nbytes / MiB / (t2 - t1),
+            "bits_per_byte": 32.0 * sum(len(c) for c in comp) / nbytes}
+
+
+def run_reference(args, cfg, rank):
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+    from model import seeded_model
+    from oracle import codec_oracle as co
+    torch.set_num_threads(os.cpu_count() or 1)
+    data = make_data(cfg, args.size)
+    arr, lens = chunk_array(data, cfg["chunks"])
+    sd = {k: v.float() for k, v in seeded_model(cfg["d"], cfg["L"]).state_dict().items()}
+    n_s, L_s = min(16, arr.shape[0]), 96
+    chunks = [arr[i, :L_s] for i in range(n_s)]
+    for _ in range(args.warmup):
+        comp, first, ls = co.compress(sd, chunks)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        comp, first, ls = co.compress(sd, chunks)
+        out = co.decompress(sd, comp, ls, first)
+        times.append(time.perf_counter() - t0)
+        assert all(np.array_equal(a, b) for a, b in zip(out, chunks))
+    nbytes = n_s * L_s
+    t = sum(times)
+    v = args.steps * nbytes / MiB / t
+    line = {"impl": "reference", "metric": "compress+decompress round-trip throughput", "value": v,
+            "unit": "MiB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000 * t / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg["name"], "sample": f"{n_s} chunks x {L_s} bytes per step"},
+            "cpu_baseline": {"value": v, "unit": "MiB/s", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"{n_s} chunks x first {L_s} bytes of the workload's chunks per step"},
+            "e2e": {"value": v, "unit": "MiB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+def run_ours(args, cfg, rank, world, local_rank, dist):
+    import numpy as np
+    import torch
+    import codec
+    from model import seeded_model
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    fmt = args.weights or cfg["fmt"]
+    data = make_data(cfg, args.size)
+    arr, lens = chunk_array(data, cfg["chunks"])
+    n, maxL = arr.shape
+    nbytes = int(sum(lens))
+    model = seeded_model(cfg["d"], cfg["L"], weight_format=fmt)
+    nm = model.native(dev)
+    X = torch.from_numpy(arr).to(dev)
+    Ld = torch.tensor(lens, dtype=torch.int32, device=dev)
+    first = X[:, 0].contiguous()
+    ws = torch.empty(nm.workspace_bytes(n), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    # warm-up (first one verifies the round trip)
+    comp_bits = None
+    for w in range(max(args.warmup, 1)):
+        words, sizes = codec.encode_device(model, X, Ld, workspace=ws)
+        out = codec.decode_device(model, words, sizes, Ld, first, max_len=maxL, workspace=ws)
+        if w == 0:
+            torch.cuda.synchronize(dev)
+            mask = torch.arange(maxL, device=dev)[None, :] < Ld[:, None]
+            if not torch.equal(out[mask], X[mask]):
+                raise RuntimeError("round trip mismatch")
+            comp_bits = int(sizes.to(torch.int64).sum().item()) * 32
+
+    # timed device-resident region
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local_rank) as clk:
+        for k in range(args.steps):
+            e0, e1, e2 = ev[k]
+            e0.record(stream)
+            words, sizes = codec.encode_device(model, X, Ld, workspace=ws)
+            e1.record(stream)
+            out = codec.decode_device(model, words, sizes, Ld, first, max_len=maxL, workspace=ws)
+            e2.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    t_c = sum(e0.elapsed_time(e1) for e0, e1, _ in ev) / 1000.0
+    t_d = sum(e1.elapsed_time(e2) for _, e1, e2 in ev) / 1000.0
+    tt = torch.tensor([t_c + t_d, t_c, t_d], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t_tot, t_c, t_d = (float(x) for x in tt.cpu())
+    value = world * args.steps * nbytes / MiB / t_tot
+
+    # end-to-end through the host API
+    e2e = None
+    if not args.no_e2e:
+        xs = [torch.from_numpy(arr[i:i + 1, :lens[i]]) for i in range(n)]
+        barrier()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        h2d = d2h = 0
+        for k in range(args.steps):
+            comp, fb, ls = codec.compress_GPU(model, xs, device=dev)
+            outs = codec.decompress_GPU(model, comp, ls, fb, device=dev)
+            h2d += nbytes + sum(4 * len(c) for c in comp)
+            d2h += sum(4 * len(c) for c in comp) + nbytes
+        torch.cuda.synchronize(dev)
+        te = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+        if dist is not None:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        if not all(np.array_equal(o[0], arr[i, :lens[i]]) for i, o in enumerate(outs)):
+            raise RuntimeError("e2e round trip mismatch")
+        e2e = {"value": world * args.steps * nbytes / MiB / float(te.item()), "unit": "MiB/s",
+               "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps}
+        barrier()
+
+    if rank != 0:
+        return
+    coded = sum(max(x - 1, 0) for x in lens)
+    alg = state_bytes_per_coded_byte(cfg["d"], cfg["L"]) * coded + nbytes + comp_bits // 8
+    per_launch = (t_c + t_d) / (2 * args.steps)
+    peak, peak_src = measured_peak()
+    tpb = traffic_per_coded_byte()
+    achieved = alg / per_launch / 1e9
+    roof = {"bound": "hbm", "kernel": "k_boa_step (fused model+quantiser+coder, one launch per direction)",
+            "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
+            "traffic": (tpb * coded if tpb else None),
+            "algorithmic_bytes_per_launch": alg,
+            "per_unit": f"{state_bytes_per_coded_byte(cfg['d'], cfg['L'])} B recurrent-state read+write per coded byte"}
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(cfg, arr, lens)
+    line = {
+        "metric": "compress+decompress round-trip throughput", "value": value, "unit": "MiB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * t_tot / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": {"tf32": "tf32 products / f32", "fp16": "fp16 products / f32",
+                                       "bf16": "bf16 products / f32"}[fmt],
+        "data": "synthetic (seeded HEP-like records, random-init seeded weights)",
+        "config": {"workload": cfg["name"], "chunks_per_gpu": n, "chunk_len": maxL, "bytes_per_gpu": nbytes,
+                   "weights": fmt, "precision": codec.PRECISION, "parallelism": f"chunk shards x{world}",
+                   "l2": "inputs larger than L2: recurrent state %d MB per pass" %
+                         (state_bytes_per_coded_byte(cfg['d'], cfg['L']) * n // 2 // 1000000)},
+        "compress_MiBps": world * args.steps * nbytes / MiB / t_c,
+        "decompress_MiBps": world * args.steps * nbytes / MiB / t_d,
+        "compress_MBps_1e6": world * args.steps * nbytes / 1e6 / t_c,
+        "decompress_MBps_1e6": world * args.steps * nbytes / 1e6 / t_d,
+        "bits_per_byte": comp_bits / nbytes,
+        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
+        "gpu_launches": 2 * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    cfg = CONFIGS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, cfg, rank)
+        return
+    dist = None
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as tdist
+        torch.cuda.set_device(local_rank)
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist = tdist
+    try:
+        run_ours(args, cfg, rank, world, local_rank, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

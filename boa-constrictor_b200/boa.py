@@ -1,0 +1,166 @@
+"""Drop-in for the reference ``boa.py``: ``BOA(device, filepath, model)`` returns
+a ``BoaFile`` with ``compress(data_path, seq_size=0, chunks_count=0,
+progress=True)``, ``decompress(progress=True) -> bytes``, ``read_from_disk()``
+and ``get_metadata()`` (boa.py:7-313), writing and reading the same ``BOA2``
+container (boa.py:47-157).
+
+Differences by design:
+  * every wave of chunks goes through the fused sm_100a codec kernel
+    (codec.encode_device / decode_device) instead of a per-byte Python loop;
+  * ``flags`` records the quantiser (bit 0) and table precision (bits 8-15);
+  * when ``torch.distributed`` is initialised with more than one rank, the
+    chunks are split into contiguous, byte-balanced ranges, one per rank (one
+    GPU per rank); each rank codes its range, the per-chunk word counts and
+    first bytes are all-gathered (the only collective), and every rank writes
+    its own payload bytes at the offsets that the gathered counts imply.
+    ``decompress`` splits the index the same way and all-gathers the decoded
+    bytes so every rank returns the whole file.
+"""
+from __future__ import annotations
+
+import os
+from pathlib import Path
+
+import numpy as np
+import torch
+
+import codec as _codec
+from boa_b200 import container as C
+from boa_b200.shard import gather_lengths, shard_range, write_sharded
+
+
+def _dist():
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        return dist
+    return None
+
+
+def BOA(device, filepath: str, model):
+    IS_CUDA = str(device).startswith("cuda") and torch.cuda.is_available()
+    if not IS_CUDA:
+        raise RuntimeError("boa_b200 runs on CUDA devices only; BOA(device='cpu', ...) has no implementation here")
+    dev = torch.device(device)
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+
+    class BoaFile:
+        MAGIC = C.MAGIC
+        IDX = C.IDX
+        VERSION = C.VERSION
+
+        def __init__(self, filepath: str, model):
+            self.filepath = Path(filepath)
+            self.model = model
+            self.compressed_data = []
+            self.first_bytes = []
+            self.lengths = []
+            self.metadata = {}
+            self.precision = _codec.PRECISION
+
+        def _model_fingerprint(self) -> bytes:
+            return C.model_fingerprint(self.model)
+
+        def _gpu_streams(self, n):
+            try:
+                s = int(os.getenv("BOA_GPU_STREAMS", "5000"))
+            except Exception:
+                s = 5000
+            return max(1, min(int(s), int(n)))
+
+        def _read_file(self):
+            data = Path(self.filepath).read_bytes()
+            p = C.parse(data)
+            self._flags = p.flags
+            payload = memoryview(data)[p.payload_start:p.index_start]
+            self.compressed_data = [bytes(payload[p.offsets[i]:p.offsets[i] + p.lengths[i]])
+                                    for i in range(p.n_chunks)]
+            self.first_bytes = p.first_bytes
+            self.lengths = p.full_lens
+            self.metadata = {"chunk_len": int(p.chunk_len), "n_chunks": int(p.n_chunks),
+                             "last_chunk_len": int(p.last_chunk_len), "uncompressed_len": int(p.uncompressed_len)}
+
+        def read_from_disk(self):
+            self._read_file()
+            print("File loaded successfully")
+
+        def get_metadata(self):
+            return dict(self.metadata)
+
+        # ------------------------------------------------------------------
+        def compress(self, data_path: str, seq_size: int = 0, chunks_count: int = 0, progress: bool = True):
+            p = Path(data_path)
+            total = p.stat().st_size
+            if total <= 0:
+                raise ValueError("Input file is empty")
+            chunk_len, n_chunks, last = C.chunking(total, seq_size, chunks_count)
+            self.metadata = {"chunk_len": chunk_len, "n_chunks": n_chunks, "uncompressed_len": int(total),
+                             "last_chunk_len": int(last if last else chunk_len)}
+            lens = [chunk_len] * (n_chunks - 1) + [last]
+            for i, ln in enumerate(lens):    # codec.py:28
+                assert ln >= 1, f"Chunk {i} must have length >= 1"
+            dist = _dist()
+            world, rank = (dist.get_world_size(), dist.get_rank()) if dist else (1, 0)
+            lo, hi = shard_range(n_chunks, world, rank)
+            mm = np.memmap(p, dtype=np.uint8, mode="r")
+            stream_n = self._gpu_streams(max(hi - lo, 1))
+            sizes_local = np.zeros(hi - lo, dtype=np.int64)
+            firsts_local = np.zeros(hi - lo, dtype=np.int64)
+            payloads = []
+            for b0 in range(lo, hi, stream_n):
+                b1 = min(b0 + stream_n, hi)
+                nb = b1 - b0
+                maxL = max(lens[b0:b1])
+                host = torch.zeros((nb, maxL), dtype=torch.uint8, pin_memory=True)
+                hv = host.numpy()
+                for j, i in enumerate(range(b0, b1)):
+                    s = i * chunk_len
+                    hv[j, :lens[i]] = mm[s:s + lens[i]]
+                firsts_local[b0 - lo:b1 - lo] = hv[:, 0]
+                X = host.to(dev, non_blocking=True)
+                L_d = torch.tensor(lens[b0:b1], dtype=torch.int32).to(dev, non_blocking=True)
+                words, sizes = _codec.encode_device(self.model, X, L_d, precision=self.precision)
+                sz = sizes.cpu().numpy().astype(np.int64)
+                wh = words.cpu().numpy().view(np.uint32)
+                sizes_local[b0 - lo:b1 - lo] = 4 * sz
+                payloads.append(b"".join(wh[j, :sz[j]].astype("<u4").tobytes() for j in range(nb)))
+            sizes_bytes, firsts = gather_lengths(dist, n_chunks, lo, hi, sizes_local, firsts_local)
+            hdr = C.header_bytes(C.make_flags(self.precision), total, chunk_len, n_chunks, last,
+                                 self._model_fingerprint())
+            write_sharded(self.filepath, hdr, lambda offs: C.index_bytes(firsts.tolist(), offs.tolist(),
+                                                                         sizes_bytes.tolist()),
+                          sizes_bytes, lo, b"".join(payloads), dist, rank)
+            self.compressed_data = []
+            self.first_bytes = [int(b) for b in firsts]
+            self.lengths = lens
+            if progress and rank == 0:
+                print(f"Compression complete: {n_chunks} chunks, chunk_len={chunk_len}, last={last}")
+
+        # ------------------------------------------------------------------
+        def decompress(self, progress: bool = True) -> bytes:
+            self._read_file()
+            bq, precision = C.flags_precision(self._flags)
+            if not bq:
+                raise ValueError("this file was coded with the reference float quantiser (flags bit 0 clear); "
+                                 "its probabilities come from other kernels and cannot be reproduced bit for bit")
+            n = len(self.compressed_data)
+            lens = self.lengths
+            dist = _dist()
+            world, rank = (dist.get_world_size(), dist.get_rank()) if dist else (1, 0)
+            lo, hi = shard_range(n, world, rank)
+            stream_n = self._gpu_streams(max(hi - lo, 1))
+            parts = []
+            for b0 in range(lo, hi, stream_n):
+                b1 = min(b0 + stream_n, hi)
+                comp = [np.frombuffer(c, dtype="<u4") for c in self.compressed_data[b0:b1]]
+                outs = _codec.decompress_GPU(self.model, comp, lens[b0:b1], self.first_bytes[b0:b1], device=dev,
+                                             precision=precision)
+                parts.extend(o.tobytes() for o in outs)
+            mine = b"".join(parts)
+            if not dist:
+                return mine
+            objs = [None] * world
+            dist.all_gather_object(objs, mine)
+            return b"".join(objs)
+
+    return BoaFile(filepath, model)

@@ -327,3 +327,56 @@ int orc_encode_cdfs(int N, int T, int K, int precision, const uint32_t* cdfs,
     }
     return status;
 }
+
+/* ------------------------------------------------------------------------- */
+/* Step-wise drivers (one symbol per stream per call), for loops whose next   */
+/* table depends on the previous decoded symbol — the shape of the            */
+/* reference's CPU codec loops (codec.py:203-235, 292-320).                   */
+/* ------------------------------------------------------------------------- */
+size_t orc_enc_state_size(void) { return sizeof(orc_enc_t); }
+size_t orc_dec_state_size(void) { return sizeof(orc_dec_t); }
+
+void orc_enc_init_n(orc_enc_t* s, int N) { for (int i = 0; i < N; ++i) orc_enc_init(&s[i]); }
+
+int orc_encode_step(int N, int K, int precision, int mode, const float* rows, const int32_t* syms,
+                    const uint8_t* mask, orc_enc_t* st, uint32_t* out, int pitch)
+{
+    uint32_t cdf[1025];
+    for (int i = 0; i < N; ++i) {
+        if (mask && !mask[i]) continue;
+        int32_t s = syms[i];
+        if (s < 0 || s >= K) continue;
+        int rc = orc_row_cdf(mode, rows + (size_t)i * K, K, precision, cdf);
+        if (rc) return rc;
+        orc_enc_put(&st[i], cdf[s], cdf[s + 1] - cdf[s], precision, out + (size_t)i * pitch, pitch);
+    }
+    return ORC_OK;
+}
+
+int orc_encode_finish_n(int N, orc_enc_t* st, uint32_t* out, int pitch, int32_t* sizes)
+{
+    int status = ORC_OK;
+    for (int i = 0; i < N; ++i) {
+        sizes[i] = orc_enc_finish(&st[i], out + (size_t)i * pitch, pitch);
+        if (st[i].overflow) status = ORC_ERR_OVERFLOW;
+    }
+    return status;
+}
+
+void orc_dec_init_n(orc_dec_t* d, int N, const uint32_t* in, int pitch, const int32_t* sizes)
+{
+    for (int i = 0; i < N; ++i) orc_dec_init(&d[i], in + (size_t)i * pitch, sizes[i]);
+}
+
+int orc_decode_step(int N, int K, int precision, int mode, const float* rows, const uint8_t* mask,
+                    orc_dec_t* d, const uint32_t* in, int pitch, const int32_t* sizes, int32_t* syms_out)
+{
+    uint32_t cdf[1025];
+    for (int i = 0; i < N; ++i) {
+        if (mask && !mask[i]) continue;
+        int rc = orc_row_cdf(mode, rows + (size_t)i * K, K, precision, cdf);
+        if (rc) return rc;
+        syms_out[i] = orc_dec_get(&d[i], cdf, K, precision, in + (size_t)i * pitch, sizes[i]);
+    }
+    return ORC_OK;
+}

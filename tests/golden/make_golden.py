@@ -1,0 +1,130 @@
+"""Regenerate the committed CPU golden fixtures in tests/golden/.
+
+Run in a container that has the reference tree (default /root/reference):
+    python tests/golden/make_golden.py [--reference /path/to/reference]
+
+Fixtures:
+  ref_container.boa / ref_container.json
+      A BOA2 file written by the reference's own BoaFile._write_file
+      (boa.py:89-112, imported from the reference tree) for fixed fake
+      payloads, plus what the reference's _read_file (boa.py:114-157) parses
+      from it and from a file written by this build's container module with
+      the quantiser flag set (the reference reader ignores flags).
+  seeded_init.json
+      sha256 of the fp32 state_dict of model.seeded_model(64, 2) (seed 0) and a
+      few sample values: pins this build's seeded Mamba-standard init.
+  oracle_c1_logits.npz
+      oracle logits (computed in fp64, stored fp32) of that model for 3 streams x 24 seeded tokens.
+  synthetic.json
+      sha256 of the config-1 input and of the first 1 MiB of the config-2 input.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import importlib.util
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "boa-constrictor_b200"))
+sys.path.insert(0, ROOT)
+
+
+def container_case():
+    rng = np.random.default_rng(123)
+    comp = [rng.integers(0, 2**32, size=k, dtype=np.uint64).astype(np.uint32) for k in (3, 0, 7, 130, 1)]
+    first = [7, 0, 255, 128, 33]
+    ulen, chunk_len, last = 5 * 1000 - 400, 1000, 600
+    return comp, first, ulen, chunk_len, last
+
+
+def load_reference_boa(reference: str):
+    sys.path.insert(0, reference)          # reference boa.py imports its own codec lazily
+    spec = importlib.util.spec_from_file_location("reference_boa", os.path.join(reference, "boa.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+class BoaBytePredictor(torch.nn.Module):
+    """Stand-in whose class name gives the reference fingerprint."""
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    a = ap.parse_args()
+    from boa_b200 import container as C
+    from model import seeded_model
+    from boa_b200 import synthetic
+    from oracle import model_oracle as mo
+
+    # --- container written by the reference ---
+    ref = load_reference_boa(a.reference)
+    comp, first, ulen, chunk_len, last = container_case()
+    path = os.path.join(HERE, "ref_container.boa")
+    bf = ref.BOA("cpu", path, BoaBytePredictor())
+    bf._write_file([c.astype("<u4").tobytes() for c in comp], first, ulen, chunk_len, last)
+    bf2 = ref.BOA("cpu", path, BoaBytePredictor())
+    bf2._read_file()
+    ours_path = os.path.join(HERE, "_ours_tmp.boa")
+    payload = b"".join(c.astype("<u4").tobytes() for c in comp)
+    sizes = [4 * len(c) for c in comp]
+    offs = [int(x) for x in np.concatenate([[0], np.cumsum(sizes)[:-1]])]
+    with open(ours_path, "wb") as f:
+        f.write(C.header_bytes(C.make_flags(16), ulen, chunk_len, len(comp), last,
+                               C.model_fingerprint(BoaBytePredictor())))
+        f.write(payload)
+        f.write(C.index_bytes(first, offs, sizes))
+    bf3 = ref.BOA("cpu", ours_path, BoaBytePredictor())
+    bf3._read_file()
+    os.remove(ours_path)
+    meta = {
+        "inputs": {"words": [c.tolist() for c in comp], "first_bytes": first, "uncompressed_len": ulen,
+                   "chunk_len": chunk_len, "last_chunk_len": last},
+        "reference_parse_of_reference_file": {"first_bytes": [int(x) for x in bf2.first_bytes],
+                                              "lengths": bf2.lengths, "metadata": bf2.metadata,
+                                              "payload_hex": [c.hex() for c in bf2.compressed_data]},
+        "reference_parse_of_our_file": {"first_bytes": [int(x) for x in bf3.first_bytes],
+                                        "lengths": bf3.lengths, "metadata": bf3.metadata,
+                                        "payload_hex": [c.hex() for c in bf3.compressed_data]},
+    }
+    with open(os.path.join(HERE, "ref_container.json"), "w") as f:
+        json.dump(meta, f, indent=1)
+
+    # --- seeded init fingerprint ---
+    m = seeded_model(64, 2)
+    sd = m.state_dict()
+    h = hashlib.sha256()
+    for k in sorted(sd):
+        h.update(k.encode())
+        h.update(sd[k].detach().float().contiguous().numpy().tobytes())
+    samples = {k: [float(x) for x in sd[k].flatten()[:3]] for k in sorted(sd)}
+    with open(os.path.join(HERE, "seeded_init.json"), "w") as f:
+        json.dump({"d_model": 64, "num_layers": 2, "seed": 0, "sha256": h.hexdigest(),
+                   "keys": sorted(sd), "first_values": samples}, f, indent=1)
+
+    # --- oracle logits ---
+    sdf = {k: v.detach().float() for k, v in sd.items()}
+    cfg = mo.config_from_state_dict(sdf)
+    toks = np.random.default_rng(9).integers(0, 256, (3, 24)).astype(np.int64)
+    lg = mo.forward(sdf, cfg, torch.from_numpy(toks), dtype=torch.float64).numpy()
+    np.savez_compressed(os.path.join(HERE, "oracle_c1_logits.npz"), tokens=toks, logits=lg.astype(np.float32))
+
+    # --- synthetic data digests ---
+    d1 = synthetic.config_data(1)
+    d2 = synthetic.hep_records(1 << 20, 2)
+    with open(os.path.join(HERE, "synthetic.json"), "w") as f:
+        json.dump({"config1_sha256": hashlib.sha256(d1).hexdigest(), "config1_len": len(d1),
+                   "hep_1MiB_seed2_sha256": hashlib.sha256(d2).hexdigest()}, f, indent=1)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,114 @@
+"""Fused codec kernel on the GPU: lossless round trips (ragged and edge-case
+chunks, reordered batches, BoaFile container), tables bit-exact with the CPU
+quantiser, compressed size against the oracle's ideal code length."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import orc
+from oracle import model_oracle as mo
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(d=64, L=2, fmt="tf32"):
+    from model import seeded_model
+    return seeded_model(d, L, weight_format=fmt)
+
+
+def _chunks(seed, lens, alphabet=256):
+    rng = np.random.default_rng(seed)
+    return [torch.from_numpy(rng.integers(0, alphabet, (1, n)).astype(np.uint8)) for n in lens]
+
+
+@pytest.mark.parametrize("fmt", ["tf32", "fp16"])
+def test_roundtrip_ragged(fmt):
+    import codec
+    m = _model(fmt=fmt)
+    lens = [1, 2, 3, 17, 100, 333, 64, 1, 250] * 3
+    xs = _chunks(1, lens)
+    comp, first, Ls = codec.compress_GPU(m, xs)
+    assert Ls == lens and first == [int(x[0, 0]) for x in xs]
+    assert len(comp[0]) == 0           # a one-byte chunk codes nothing (boa stores byte 0 raw)
+    outs = codec.decompress_GPU(m, comp, Ls, first)
+    for x, o in zip(xs, outs):
+        assert np.array_equal(x.numpy(), o)
+
+
+def test_decode_in_another_batch_order():
+    """Probabilities do not depend on which chunks share a CTA: decode a
+    permuted subset of what was encoded together."""
+    import codec
+    m = _model()
+    lens = [40 + 7 * i for i in range(37)]
+    xs = _chunks(2, lens)
+    comp, first, Ls = codec.compress_GPU(m, xs)
+    idx = list(range(36, -1, -2)) + [5]
+    outs = codec.decompress_GPU(m, [comp[i] for i in idx], [Ls[i] for i in idx], [first[i] for i in idx])
+    for j, i in enumerate(idx):
+        assert np.array_equal(xs[i].numpy(), outs[j])
+
+
+def test_stream_matches_cpu_coder_on_gpu_logits():
+    """The in-kernel quantiser + coder equal the CPU oracle coder run on the
+    kernel's own logits (tables bit-exact, bitstream bit-exact)."""
+    import codec
+    m = _model()
+    lens = [30, 55, 9]
+    xs = _chunks(3, lens)
+    comp, first, Ls = codec.compress_GPU(m, xs)
+    maxL = max(lens)
+    toks = np.zeros((3, maxL), np.int64)
+    for i, x in enumerate(xs):
+        toks[i, :lens[i]] = x.numpy()[0]
+    lg = m(torch.from_numpy(toks).cuda()).cpu().numpy()        # logits for next byte
+    rows = lg[:, :-1]                                           # predict byte t from prefix < t
+    syms = toks[:, 1:].astype(np.int32)
+    counts = np.array([n - 1 for n in lens], np.int32)
+    w, s, st = orc.encode(rows, syms, counts, 16, orc.MODE_BQ, pitch=64)
+    assert st == 0
+    for i in range(3):
+        assert np.array_equal(comp[i], w[i, :s[i]]), i
+
+
+def test_boafile_roundtrip_config1(tmp_path):
+    from boa import BOA
+    from boa_b200 import synthetic
+    data = synthetic.config_data(1)[:96 * 1024]
+    src = tmp_path / "in.bin"; src.write_bytes(data)
+    m = _model()
+    bf = BOA("cuda", str(tmp_path / "out.boa"), m)
+    bf.compress(str(src), chunks_count=16, progress=False)
+    out = BOA("cuda", str(tmp_path / "out.boa"), m).decompress(progress=False)
+    assert out == data
+    meta = bf.get_metadata()
+    assert meta["n_chunks"] == 16 and meta["uncompressed_len"] == len(data)
+
+
+def test_compressed_size_vs_oracle_ideal():
+    """Code length within 0.5% of the oracle's ideal -sum log2 p (fp64 model,
+    exact softmax) over the coded bytes, plus the 2-3 flush words per chunk."""
+    import codec
+    from boa_b200 import synthetic
+    m = _model()
+    data = np.frombuffer(synthetic.config_data(1)[:8 * 2048], dtype=np.uint8).reshape(8, 2048)
+    xs = [torch.from_numpy(r.copy()).reshape(1, -1) for r in data]
+    comp, first, Ls = codec.compress_GPU(m, xs)
+    bits = sum(32 * len(c) for c in comp)
+    sd = {k: v.float() for k, v in m.state_dict().items()}
+    lg = mo.forward(sd, mo.config_from_state_dict(sd), torch.from_numpy(data.astype(np.int64)), dtype=torch.float64)
+    lp = torch.log_softmax(lg[:, :-1], -1).gather(-1, torch.from_numpy(data[:, 1:].astype(np.int64))[..., None])
+    ideal = float(-lp.sum() / np.log(2))
+    assert bits <= ideal * 1.005 + 8 * 96, (bits, ideal)
+
+
+def test_pitch_overflow_is_an_error():
+    import codec
+    from boa_b200._native import BoaError
+    m = _model()
+    x = torch.randint(0, 256, (4, 500), dtype=torch.uint8).cuda()
+    lens = torch.full((4,), 500, dtype=torch.int32).cuda()
+    with pytest.raises(BoaError):
+        codec.encode_device(m, x, lens, pitch_words=8)
