@@ -12,7 +12,8 @@ import os
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libboa_b200.so")
+# BOA_B200_LIB overrides the library path (e.g. a build with BOA_PHASE_PROFILE)
+LIB_PATH = os.environ.get("BOA_B200_LIB") or os.path.join(_HERE, "libboa_b200.so")
 
 BOA_OK = 0
 BOA_ERR_ARG = 1

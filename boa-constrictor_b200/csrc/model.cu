@@ -35,6 +35,8 @@
 #include <cstdint>
 #include <cstring>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <string>
 #include <vector>
 
@@ -48,8 +50,7 @@ namespace boa {
 constexpr int kTileBytes = 16384;      // one A tile: 128 rows x 128 bytes
 constexpr int kComputeThreads = 512;   // warps 2..17
 constexpr int kThreads = 576;
-constexpr int kStages = 4;             // weight ring depth
-constexpr int kCT = 16;                // chunks per CTA (MMA N)
+constexpr int kCT = 16;                // chunks per CTA of the diagnostic GEMM
 constexpr long long kWaitBudget = 4000000000LL;  // SM clock cycles per bounded wait (~2 s)
 
 enum StepMode : int { MODE_ENCODE = 0, MODE_DECODE = 1, MODE_LOGITS = 2 };
@@ -106,6 +107,14 @@ struct StepArgs {
   const uint8_t* wtiles; const float* params;
   float4* conv_state; float4* ssm_state;
   uint32_t* err;
+  unsigned long long* prof;   // optional per-phase SM-cycle totals of CTA 0 (BOA_PHASE_PROFILE)
+};
+
+// Phase slots of the optional profile (see boa_b200/_native.py PHASES).
+enum ProfSlot : int {
+  PF_EMBED = 0, PF_LN1, PF_W_IN, PF_CONV, PF_W_XP, PF_XP, PF_W_DT, PF_SCAN, PF_W_OUT, PF_LN2, PF_W_FF1, PF_FF1,
+  PF_W_FF2, PF_FF2, PF_HEAD0, PF_W_H0, PF_HEAD1, PF_W_H2, PF_HEAD2, PF_CODER,
+  PF_MMA_WAIT_FULL = 24, PF_MMA_WAIT_ACT, PF_MMA_TOTAL, PF_PROD_WAIT_EMPTY, PF_TILES, PF_STEPS, PF_SLOTS = 32
 };
 
 // ------------------------------ device math ---------------------------------
@@ -117,34 +126,66 @@ __device__ __forceinline__ void cbar_sync() {   // named barrier over the 512 co
   asm volatile("bar.sync 1, 512;" ::: "memory");
 }
 
-// Shared-memory carve-up (dynamic smem, base rounded up to 1024 bytes).
+// Chunks per CTA (the MMA N) is 16 or 32.  A tcgen05.mma with M = 128 costs
+// about the same for any N <= 128 (the weight tile read dominates), so more
+// chunks per CTA amortise the weight stream; 32 fits TMEM and shared memory
+// with 16-bit operands and d_model <= 256.  The host picks 32 only when there
+// are enough chunks to keep every SM busy.
 template <int D, int KIND>
-struct Smem {
-  static constexpr int CT = kCT;
-  static constexpr int EB = tc::OpKind<KIND>::kElemBytes;
-  static constexpr int F = 4 * D;
-  static constexpr int RING = kStages * kTileBytes;
-  static constexpr int BBUF = CT * F * EB;                  // largest K is F
-  static constexpr int HRES = CT * D * 4;
-  static constexpr int SCR = CT * (D > 256 ? D : 256) * 4;  // LN2 input / logits
-  static constexpr int DBCB = CT * 64 * 4;
-  static constexpr int o_ring = 0;
-  static constexpr int o_bbuf = o_ring + RING;
-  static constexpr int o_hres = o_bbuf + BBUF;
-  static constexpr int o_scr = o_hres + HRES;
-  static constexpr int o_dbc = o_scr + SCR;
-  static constexpr int o_enc = o_dbc + DBCB;                 // RcEnc / RcDec [CT]
-  static constexpr int o_prev = o_enc + CT * 32;
-  static constexpr int o_bars = o_prev + CT * 4;             // full[S], empty[S], mma, act, drain
-  static constexpr int o_misc = o_bars + (2 * kStages + 3) * 8;
-  static constexpr int TOTAL = o_misc + 64;
-  static constexpr int ALLOC = TOTAL + 1024;
+struct ChunkTileMax {
+  static constexpr int value = (KIND != 0 && D <= 256) ? 32 : 16;
 };
 
+// Shared-memory carve-up (dynamic smem, base rounded up to 1024 bytes).  The
+// fp32 scratch (LN2 input / logits) lives in the upper part of the operand
+// buffer when it fits: whenever it is written, the operand there (the
+// out_proj input y or the head.2 input) has already been consumed.
+template <int D, int KIND, int CT_>
+struct Smem {
+  static constexpr int CT = CT_;
+  static constexpr int EB = tc::OpKind<KIND>::kElemBytes;
+  static constexpr int E = 2 * D, F = 4 * D;
+  static constexpr int BBUF = CT * F * EB;                  // largest K is F
+  static constexpr int Y_BYTES = CT * E * EB;               // out_proj input (also covers LN2 / head inputs)
+  static constexpr int SCR = CT * (D > 256 ? D : 256) * 4;  // LN2 input / logits (fp32)
+  static constexpr bool SCR_ALIAS = BBUF - Y_BYTES >= SCR;
+  static constexpr int HRES = CT * D * 4;
+  static constexpr int DBCB = CT * 64 * 4;
+  static constexpr int o_bbuf = 0;
+  static constexpr int o_scr = SCR_ALIAS ? Y_BYTES : BBUF;
+  static constexpr int o_hres = SCR_ALIAS ? BBUF : BBUF + SCR;
+  static constexpr int o_dbc = o_hres + HRES;
+  static constexpr int o_enc = o_dbc + DBCB;                 // RcEnc / RcDec [CT]
+  static constexpr int o_prev = o_enc + CT * 32;
+  static constexpr int o_lens = o_prev + CT * 4;
+  static constexpr int o_bars = o_lens + CT * 4;
+  static constexpr int kMaxStages = 12;
+  static constexpr int o_misc = o_bars + (2 * kMaxStages + 3) * 8;
+  static constexpr int o_prof = o_misc + 64;                 // PF_SLOTS x u64 phase accumulators
+  static constexpr int o_ring = ((o_prof + 256 + 1023) / 1024) * 1024;
+  static constexpr int kBudget = 227 * 1024 - 1024;          // minus alignment slack
+  static constexpr int STAGES_FIT = (kBudget - o_ring) / kTileBytes;
+  static constexpr int STAGES = STAGES_FIT > kMaxStages ? kMaxStages : STAGES_FIT;
+  static constexpr int TOTAL = o_ring + STAGES * kTileBytes;
+  static constexpr int ALLOC = TOTAL + 1024;
+  static_assert(STAGES >= 3, "not enough shared memory for the weight ring");
+};
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 // -------------------------------- the kernel --------------------------------
-template <int D, int KIND>
+template <int D, int KIND, int CT_>
 __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant__ StepArgs a) {
-  constexpr int CT = kCT;
+  using S = Smem<D, KIND, CT_>;
+  using LP = LayerParams<D>;
+  constexpr int CT = S::CT;
+  constexpr int NG = CT / 8;                             // groups of 8 chunks
+  constexpr int kStagesK = S::STAGES;
   constexpr int E = 2 * D, R = (D + 15) / 16, DBC = R + 32, F = 4 * D;
   constexpr int PER = 128 / tc::OpKind<KIND>::kElemBytes;
   constexpr int kD = D / PER, kE = E / PER, kF = F / PER;
@@ -154,8 +195,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   static_assert(MT_F * CT <= 512, "TMEM budget (ff.0)");
   static_assert(R <= PER && DBC <= 64, "x_proj outputs must fit one tile / one K slice");
   static_assert(D % 32 == 0 && D >= 64, "d_model");
-  using S = Smem<D, KIND>;
-  using LP = LayerParams<D>;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -165,15 +204,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   float* scr = reinterpret_cast<float*>(smem + S::o_scr);
   float* dbc = reinterpret_cast<float*>(smem + S::o_dbc);
   int32_t* prev = reinterpret_cast<int32_t*>(smem + S::o_prev);
+  int32_t* lens_sh = reinterpret_cast<int32_t*>(smem + S::o_lens);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::o_bars);
-  uint64_t* empty = full + kStages;
-  uint64_t* mma_bar = empty + kStages;
+  uint64_t* empty = full + S::kMaxStages;
+  uint64_t* mma_bar = empty + S::kMaxStages;
   uint64_t* act_bar = mma_bar + 1;
   uint64_t* drain_bar = act_bar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::o_misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::o_misc + 4);
   int* nsteps_sh = reinterpret_cast<int*>(smem + S::o_misc + 8);
   volatile int* cons_sh = reinterpret_cast<volatile int*>(smem + S::o_misc + 12);
+  volatile long long* prod_it_sh = reinterpret_cast<volatile long long*>(smem + S::o_misc + 16);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -189,12 +230,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
 
   // ------------------------------- setup -------------------------------
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
+    for (int s = 0; s < kStagesK; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
     tc::mbar_init(mma_bar, 1);
     tc::mbar_init(act_bar, kComputeThreads);
     tc::mbar_init(drain_bar, 1);
     *abort_flag = 0;
     *cons_sh = 0;
+    *prod_it_sh = 0;
     int ns = 0;
     if (mode == MODE_LOGITS) {
       ns = a.n_steps;
@@ -214,22 +256,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   if (tid >= 64 && tid < 64 + CT) {
     const int n = tid - 64;
     const int c = c0 + n;
-    int p0 = 0;
+    int p0 = 0, len = 0;
     if (c < a.n_chunks) {
       if (mode == MODE_ENCODE) {
+        len = a.lens[c];
         p0 = a.bytes[(long long)c * a.in_pitch];
         rc_enc_reset(reinterpret_cast<RcEnc*>(smem + S::o_enc)[n]);
       } else if (mode == MODE_DECODE) {
+        len = a.lens[c];
         p0 = a.first_bytes[c];
         int nw = a.sizes_in[c];
         nw = nw < 0 ? 0 : (nw > a.pitch_words ? a.pitch_words : nw);
         rc_dec_reset(reinterpret_cast<RcDec*>(smem + S::o_enc)[n], a.words_in + (long long)c * a.pitch_words, nw);
         a.out[(long long)c * a.out_pitch] = (uint8_t)p0;
       } else {
+        len = 0x7fffffff;
         p0 = a.tokens[(long long)c * a.n_steps];
       }
     }
     prev[n] = (p0 >= 0 && p0 < V) ? p0 : 0;
+    lens_sh[n] = len;     // 0 marks a padding column (no chunk)
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -242,57 +288,75 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
     if (lane == 0 && nsteps > 0) {
       const uint64_t pol = tc::policy_evict_last();
       long long it = 0;
+      int st = 0;
+      uint32_t ph = 0;
       bool ok = true;
+      #ifdef BOA_PHASE_PROFILE
+      const bool prof = a.prof != nullptr && blockIdx.x == 0;
+#else
+      constexpr bool prof = false;
+#endif
+      unsigned long long w_empty = 0;
       for (int s = 0; s < nsteps && ok; ++s) {
-        for (int t = 0; t < a.tiles_per_step; ++t, ++it) {
-          const int st = (int)(it % kStages);
-          const uint32_t round = (uint32_t)(it / kStages);
-          if (!tc::mbar_wait(&empty[st], (round & 1u) ^ 1u, abort_flag, kWaitBudget)) { ok = false; break; }
+        const uint8_t* src = a.wtiles;
+        for (int t = 0; t < a.tiles_per_step; ++t, ++it, src += kTileBytes) {
+          const long long tw = prof ? clock64() : 0;
+          if (!tc::mbar_wait(&empty[st], ph ^ 1u, abort_flag, kWaitBudget)) { ok = false; break; }
+          if (prof) w_empty += clock64() - tw;
           tc::mbar_arrive_expect_tx(&full[st], kTileBytes);
-          tc::bulk_g2s(ring + st * kTileBytes, a.wtiles + (long long)t * kTileBytes, kTileBytes, &full[st], pol);
+          tc::bulk_g2s(ring + st * kTileBytes, src, kTileBytes, &full[st], pol);
+          if (++st == kStagesK) { st = 0; ph ^= 1u; }
         }
       }
-      // every issued copy must land before the CTA may exit
-      for (long long j = *cons_sh; j < it; ++j) {
-        const int st = (int)(j % kStages);
-        const uint32_t round = (uint32_t)(j / kStages);
-        const long long t0 = clock64();
-        while (!tc::mbar_try_wait(&full[st], round & 1u)) {
-          if (clock64() - t0 > kWaitBudget) break;
-        }
-      }
+      if (prof) a.prof[PF_PROD_WAIT_EMPTY] = w_empty;
+      *prod_it_sh = it;   // copies issued; teardown drains the unconsumed ones on abort
     }
   } else if (warp == 1) {
     // ============================= MMA issuer =============================
     if (lane == 0 && nsteps > 0) {
       const uint32_t id = tc::idesc<KIND>(128, CT);
-      const uint32_t bbase = tc::smem_u32(bbuf);
-      const uint32_t rbase = tc::smem_u32(ring);
+      const uint64_t adesc0 = tc::sdesc_sw128(tc::smem_u32(ring));
+      const uint64_t bdesc0 = tc::sdesc_sw128(tc::smem_u32(bbuf));
+      constexpr uint64_t kTileDesc = kTileBytes >> 4;      // descriptor start-address units (16 B)
+      constexpr uint64_t kSliceDesc = (CT * 128) >> 4;
       long long it = 0;
+      int st = 0;
+      uint32_t ph = 0;
       uint32_t act_phase = 0;
       bool ok = true;
+      #ifdef BOA_PHASE_PROFILE
+      const bool prof = a.prof != nullptr && blockIdx.x == 0;
+#else
+      constexpr bool prof = false;
+#endif
+      unsigned long long w_full = 0, w_act = 0;
+      const long long t_mma0 = clock64();
       // D[col0 + mt*CT ...] = sum over ks of A(mt, ks) * B(ks)^T
       auto gemm = [&](int n_mt, int n_ks, int col0) -> bool {
-        for (int mt = 0; mt < n_mt; ++mt) {
-          for (int ks = 0; ks < n_ks; ++ks, ++it) {
-            const int st = (int)(it % kStages);
-            const uint32_t round = (uint32_t)(it / kStages);
-            if (!tc::mbar_wait(&full[st], round & 1u, abort_flag, kWaitBudget)) return false;
+        uint32_t dcol = tmem + (uint32_t)col0;
+        for (int mt = 0; mt < n_mt; ++mt, dcol += CT) {
+          uint64_t bd = bdesc0;
+          for (int ks = 0; ks < n_ks; ++ks, bd += kSliceDesc) {
+            const long long tw = prof ? clock64() : 0;
+            if (!tc::mbar_wait(&full[st], ph, abort_flag, kWaitBudget)) return false;
+            if (prof) w_full += clock64() - tw;
             tc::tc_fence_after();
-            const uint32_t a0 = rbase + st * kTileBytes;
-            const uint32_t b0 = bbase + ks * CT * 128;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              tc::mma<KIND>(tmem + (uint32_t)(col0 + mt * CT), tc::sdesc_sw128(a0 + kk * 32),
-                            tc::sdesc_sw128(b0 + kk * 32), id, (ks > 0 || kk > 0) ? 1u : 0u);
+            const uint64_t ad = adesc0 + (uint64_t)st * kTileDesc;
+            tc::mma<KIND>(dcol, ad, bd, id, ks > 0 ? 1u : 0u);
+            tc::mma<KIND>(dcol, ad + 2, bd + 2, id, 1u);       // +32 bytes of K
+            tc::mma<KIND>(dcol, ad + 4, bd + 4, id, 1u);
+            tc::mma<KIND>(dcol, ad + 6, bd + 6, id, 1u);
             tc::mma_commit(&empty[st]);
-            *cons_sh = (int)(it + 1);
+            *cons_sh = (int)(++it);
+            if (++st == kStagesK) { st = 0; ph ^= 1u; }
           }
         }
         return true;
       };
       auto step_gemm = [&](int n_mt, int n_ks, int col0) -> bool {
+        const long long tw = prof ? clock64() : 0;
         if (!tc::mbar_wait(act_bar, act_phase, abort_flag, kWaitBudget)) return false;
+        if (prof) w_act += clock64() - tw;
         act_phase ^= 1u;
         tc::tc_fence_after();
         if (!gemm(n_mt, n_ks, col0)) return false;
@@ -310,6 +374,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         }
         ok = ok && step_gemm(MT_D, kD, 0)          // head.0
              && step_gemm(2, kD, 0);               // head.2
+      }
+      if (prof) {
+        a.prof[PF_MMA_WAIT_FULL] = w_full;
+        a.prof[PF_MMA_WAIT_ACT] = w_act;
+        a.prof[PF_MMA_TOTAL] = clock64() - t_mma0;
+        a.prof[PF_TILES] = (unsigned long long)it;
+        a.prof[PF_STEPS] = (unsigned long long)nsteps;
       }
       // every issued MMA must retire before TMEM is released
       tc::mma_commit(drain_bar);
@@ -329,6 +400,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
     uint32_t mma_phase = 0;
     RcEnc* encs = reinterpret_cast<RcEnc*>(smem + S::o_enc);
     RcDec* decs = reinterpret_cast<RcDec*>(smem + S::o_enc);
+#ifdef BOA_PHASE_PROFILE
+    const bool pon = a.prof != nullptr && blockIdx.x == 0 && ct == 0;
+    unsigned long long* pacc = reinterpret_cast<unsigned long long*>(smem + S::o_prof);
+    if (pon) for (int i = 0; i < 20; ++i) pacc[i] = 0;
+    long long tlast = clock64();
+    auto mark = [&](int slot) {
+      if (pon) { const long long now = clock64(); pacc[slot] += (unsigned long long)(now - tlast); tlast = now; }
+    };
+#else
+    auto mark = [](int) {};
+#endif
 
     auto arrive_act = [&]() {
       tc::fence_proxy_async_smem();
@@ -342,12 +424,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       cbar_sync();
       tc::tc_fence_after();
       return *abort_flag == 0;
-    };
-    auto is_active = [&](int n, int t) -> bool {
-      const int c = c0 + n;
-      if (c >= a.n_chunks) return false;
-      if (mode == MODE_LOGITS) return true;
-      return t < a.lens[c];
     };
     // LayerNorm (eps 1e-5, biased variance, two passes) of CT rows of `src`
     // (fp32 [CT][D]) into the B operand; a warp per chunk.
@@ -379,147 +455,209 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
     for (int s = 0; s < nsteps && ok; ++s) {
       const int t = (mode == MODE_LOGITS) ? s : s + 1;     // position predicted / coded
       const bool load_state = !(a.fresh && s == 0);
+      // active mask of this step (bit n: chunk n codes position t)
+      uint32_t amask = 0;
+#pragma unroll
+      for (int n = 0; n < CT; ++n) amask |= (t < lens_sh[n] ? 1u : 0u) << n;
+      const uint32_t lmask = load_state ? amask : 0u;
       // ---- embedding
       for (int i = ct; i < CT * D; i += kComputeThreads) {
         const int n = i / D, f = i - (i / D) * D;
         hres[i] = __ldg(P + o_emb + (long long)prev[n] * D + f);
       }
       cbar_sync();
+      mark(PF_EMBED);
       for (int l = 0; l < L && ok; ++l) {
         const float* lp = P + (long long)LP::stride * l;
         // ---- LN1 -> B ; in_proj
         layernorm_to_b(hres, lp + LP::ln1w, lp + LP::ln1b);
         arrive_act();
+        mark(PF_LN1);
         if (!(ok = wait_mma())) break;
-        // ---- causal conv (width 4) + SiLU, thread per channel; xc -> B and TMEM
+        mark(PF_W_IN);
+        // ---- causal conv (width 4) + SiLU, thread per channel; xc -> B and TMEM.
+        //      The next 8 chunks' windows load while the current 8 compute.
         for (int mt = g; mt < MT_E; mt += 4) {
           const int e = mt * 128 + row;
-          float xv[16];
-          tc::tmem_ld16(tq + (uint32_t)(COL_X + mt * CT), xv);
           const float4 w = __ldg(reinterpret_cast<const float4*>(lp + LP::convw) + e);
           const float cb = __ldg(lp + LP::convb + e);
-#pragma unroll 4
-          for (int n = 0; n < CT; ++n) {
-            const bool act = is_active(n, t);
-            const long long si = ((long long)(c0 + n) * L + l) * E + e;
-            float4 st = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (act && load_state) st = a.conv_state[si];
-            float acc = cb;
-            acc = fmaf(w.x, st.x, acc);
-            acc = fmaf(w.y, st.y, acc);
-            acc = fmaf(w.z, st.z, acc);
-            acc = fmaf(w.w, xv[n], acc);
-            const float xc = silu_f(acc);
-            if (act) a.conv_state[si] = make_float4(st.y, st.z, xv[n], 0.f);
-            tc::store_operand<KIND>(bbuf, n, e, CT, xc);
-            xv[n] = xc;
+          float4* cs = a.conv_state + ((long long)c0 * L + l) * E + e;   // chunk stride L*E
+          const long long cst = (long long)L * E;
+          float4 nx[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) nx[j] = ((lmask >> j) & 1u) ? cs[j * cst] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+          for (int gi = 0; gi < NG; ++gi) {
+            float4 st[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) st[j] = nx[j];
+            if (gi + 1 < NG) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int n = 8 * (gi + 1) + j;
+                nx[j] = ((lmask >> n) & 1u) ? cs[n * cst] : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+            }
+            float xv[8];
+            const uint32_t col = (uint32_t)(COL_X + mt * CT + 8 * gi);
+            tc::tmem_ld8(tq + col, xv);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int n = 8 * gi + j;
+              float acc = cb;
+              acc = fmaf(w.x, st[j].x, acc);
+              acc = fmaf(w.y, st[j].y, acc);
+              acc = fmaf(w.z, st[j].z, acc);
+              acc = fmaf(w.w, xv[j], acc);
+              const float xc = silu_fast(acc);
+              if ((amask >> n) & 1u) cs[n * cst] = make_float4(st[j].y, st[j].z, xv[j], 0.f);
+              tc::store_operand<KIND>(bbuf, n, e, CT, xc);
+              xv[j] = xc;
+            }
+            tc::tmem_st8(tq + col, xv);
           }
-          tc::tmem_st16(tq + (uint32_t)(COL_X + mt * CT), xv);
+          tc::tmem_wait_st();
         }
         arrive_act();
+        mark(PF_CONV);
         if (!(ok = wait_mma())) break;
+        mark(PF_W_XP);
         // ---- x_proj epilogue: dt_r -> B (K slice 0, zero padded), B/C -> smem
         if (g == 0) {
-          float v[16];
-          tc::tmem_ld16(tq + (uint32_t)COL_XP, v);
-          if (row < DBC) {
+#pragma unroll 1
+          for (int gi = 0; gi < NG; ++gi) {
+            float v[8];
+            tc::tmem_ld8(tq + (uint32_t)(COL_XP + 8 * gi), v);
+            if (row < DBC) {
 #pragma unroll
-            for (int n = 0; n < CT; ++n) dbc[n * 64 + row] = v[n];
-          }
-          if (row < PER) {
+              for (int j = 0; j < 8; ++j) dbc[(8 * gi + j) * 64 + row] = v[j];
+            }
+            if (row < PER) {
 #pragma unroll
-            for (int n = 0; n < CT; ++n) tc::store_operand<KIND>(bbuf, n, row, CT, row < R ? v[n] : 0.f);
+              for (int j = 0; j < 8; ++j) tc::store_operand<KIND>(bbuf, 8 * gi + j, row, CT, row < R ? v[j] : 0.f);
+            }
           }
         }
         arrive_act();
+        mark(PF_XP);
         if (!(ok = wait_mma())) break;
-        // ---- selective scan + D skip + SiLU(z) gate, thread per channel
+        mark(PF_W_DT);
+        // ---- selective scan + D skip + SiLU(z) gate, thread per channel; the
+        //      next chunk's state loads while the current one computes, and
+        //      A*log2(e) is re-read from L1 per chunk to keep registers free
         for (int mt = g; mt < MT_E; mt += 4) {
           const int e = mt * 128 + row;
-          float xc[16], z[16], dtr[16];
-          tc::tmem_ld16(tq + (uint32_t)(COL_X + mt * CT), xc);
-          tc::tmem_ld16(tq + (uint32_t)(COL_Z + mt * CT), z);
-          tc::tmem_ld16(tq + (uint32_t)(COL_DT + mt * CT), dtr);
-          float A2[16];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float4 t4 = __ldg(reinterpret_cast<const float4*>(lp + LP::A2) + e * 4 + j);
-            A2[4 * j] = t4.x; A2[4 * j + 1] = t4.y; A2[4 * j + 2] = t4.z; A2[4 * j + 3] = t4.w;
-          }
+          const float4* A2p = reinterpret_cast<const float4*>(lp + LP::A2) + e * 4;
           const float Dp = __ldg(lp + LP::Dp + e);
           const float bdt = __ldg(lp + LP::dtb + e);
-          for (int n = 0; n < CT; ++n) {
-            const bool act = is_active(n, t);
-            const long long si = (((long long)(c0 + n) * L + l) * E + e) * 4;
-            float h[16];
-            if (act && load_state) {
+          float4* ss = a.ssm_state + (((long long)c0 * L + l) * E + e) * 4;   // chunk stride L*E*4
+          const long long cstride = (long long)L * E * 4;
+          float4 nx[4];
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float4 t4 = a.ssm_state[si + j];
-                h[4 * j] = t4.x; h[4 * j + 1] = t4.y; h[4 * j + 2] = t4.z; h[4 * j + 3] = t4.w;
+          for (int k = 0; k < 4; ++k) nx[k] = (lmask & 1u) ? ss[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+          for (int gi = 0; gi < CT / 4; ++gi) {
+            float xc[4], z[4], dtr[4];
+            tc::tmem_ld4(tq + (uint32_t)(COL_X + mt * CT + 4 * gi), xc);
+            tc::tmem_ld4(tq + (uint32_t)(COL_Z + mt * CT + 4 * gi), z);
+            tc::tmem_ld4(tq + (uint32_t)(COL_DT + mt * CT + 4 * gi), dtr);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int n = 4 * gi + j;
+              float h[16];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                h[4 * k] = nx[k].x; h[4 * k + 1] = nx[k].y; h[4 * k + 2] = nx[k].z; h[4 * k + 3] = nx[k].w;
               }
-            } else {
+              if (n + 1 < CT) {
 #pragma unroll
-              for (int j = 0; j < 16; ++j) h[j] = 0.f;
-            }
-            const float dtv = softplus_f(dtr[n] + bdt);
-            const float dx = dtv * xc[n];
-            const float* bc = dbc + n * 64 + R;
-            float y = 0.f;
+                for (int k = 0; k < 4; ++k)
+                  nx[k] = ((lmask >> (n + 1)) & 1u) ? ss[(n + 1) * cstride + k] : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+              const float dtv = softplus_f(dtr[j] + bdt);
+              const float dx = dtv * xc[j];
+              const float4* bc4 = reinterpret_cast<const float4*>(dbc + n * 64 + R);
+              float y = 0.f;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              h[j] = fmaf(h[j], exp2f(dtv * A2[j]), dx * bc[j]);
-              y = fmaf(h[j], bc[16 + j], y);
-            }
-            if (act) {
+              for (int k = 0; k < 4; ++k) {
+                const float4 A4 = __ldg(A2p + k);
+                const float4 B4 = bc4[k];
+                const float4 C4 = bc4[4 + k];
+                h[4 * k + 0] = fmaf(h[4 * k + 0], ex2_approx(dtv * A4.x), dx * B4.x);
+                h[4 * k + 1] = fmaf(h[4 * k + 1], ex2_approx(dtv * A4.y), dx * B4.y);
+                h[4 * k + 2] = fmaf(h[4 * k + 2], ex2_approx(dtv * A4.z), dx * B4.z);
+                h[4 * k + 3] = fmaf(h[4 * k + 3], ex2_approx(dtv * A4.w), dx * B4.w);
+                y = fmaf(h[4 * k + 0], C4.x, y);
+                y = fmaf(h[4 * k + 1], C4.y, y);
+                y = fmaf(h[4 * k + 2], C4.z, y);
+                y = fmaf(h[4 * k + 3], C4.w, y);
+              }
+              if ((amask >> n) & 1u) {
 #pragma unroll
-              for (int j = 0; j < 4; ++j)
-                a.ssm_state[si + j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+                for (int k = 0; k < 4; ++k)
+                  ss[n * cstride + k] = make_float4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
+              }
+              y = fmaf(Dp, xc[j], y);
+              y *= silu_fast(z[j]);
+              tc::store_operand<KIND>(bbuf, n, e, CT, y);
             }
-            y = fmaf(Dp, xc[n], y);
-            y *= silu_f(z[n]);
-            tc::store_operand<KIND>(bbuf, n, e, CT, y);
           }
         }
         arrive_act();
+        mark(PF_SCAN);
         if (!(ok = wait_mma())) break;
+        mark(PF_W_OUT);
         // ---- out_proj epilogue -> scratch, then LN2 -> B
         if (g < MT_D) {
-          float v[16];
-          tc::tmem_ld16(tq + (uint32_t)(g * CT), v);
           const int f = g * 128 + row;
-          if (f < D) {
+#pragma unroll 1
+          for (int gi = 0; gi < NG; ++gi) {
+            float v[8];
+            tc::tmem_ld8(tq + (uint32_t)(g * CT + 8 * gi), v);
+            if (f < D) {
 #pragma unroll
-            for (int n = 0; n < CT; ++n) scr[n * D + f] = v[n];
+              for (int j = 0; j < 8; ++j) scr[(8 * gi + j) * D + f] = v[j];
+            }
           }
         }
         cbar_sync();
         layernorm_to_b(scr, lp + LP::ln2w, lp + LP::ln2b);
         arrive_act();
+        mark(PF_LN2);
         if (!(ok = wait_mma())) break;
+        mark(PF_W_FF1);
         // ---- ff.0 epilogue: + b1, exact GELU -> B
         for (int mt = g; mt < MT_F; mt += 4) {
-          float v[16];
-          tc::tmem_ld16(tq + (uint32_t)(mt * CT), v);
           const int f = mt * 128 + row;
           const float b = __ldg(lp + LP::b1 + f);
+#pragma unroll 1
+          for (int gi = 0; gi < NG; ++gi) {
+            float v[8];
+            tc::tmem_ld8(tq + (uint32_t)(mt * CT + 8 * gi), v);
 #pragma unroll
-          for (int n = 0; n < CT; ++n) tc::store_operand<KIND>(bbuf, n, f, CT, gelu_f(v[n] + b));
+            for (int j = 0; j < 8; ++j) tc::store_operand<KIND>(bbuf, 8 * gi + j, f, CT, gelu_f(v[j] + b));
+          }
         }
         arrive_act();
+        mark(PF_FF1);
         if (!(ok = wait_mma())) break;
+        mark(PF_W_FF2);
         // ---- ff.2 epilogue: residual update
         if (g < MT_D) {
-          float v[16];
-          tc::tmem_ld16(tq + (uint32_t)(g * CT), v);
           const int f = g * 128 + row;
-          if (f < D) {
-            const float b = __ldg(lp + LP::b2 + f);
+          const float b = f < D ? __ldg(lp + LP::b2 + f) : 0.f;
+#pragma unroll 1
+          for (int gi = 0; gi < NG; ++gi) {
+            float v[8];
+            tc::tmem_ld8(tq + (uint32_t)(g * CT + 8 * gi), v);
+            if (f < D) {
 #pragma unroll
-            for (int n = 0; n < CT; ++n) hres[n * D + f] += v[n] + b;
+              for (int j = 0; j < 8; ++j) hres[(8 * gi + j) * D + f] += v[j] + b;
+            }
           }
         }
         cbar_sync();
+        mark(PF_FF2);
       }
       if (!ok) break;
       // ---- head.0: Linear + ReLU
@@ -528,33 +666,44 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         tc::store_operand<KIND>(bbuf, n, f, CT, hres[i]);
       }
       arrive_act();
+      mark(PF_HEAD0);
       if (!(ok = wait_mma())) break;
+      mark(PF_W_H0);
       if (g < MT_D) {
-        float v[16];
-        tc::tmem_ld16(tq + (uint32_t)(g * CT), v);
         const int f = g * 128 + row;
-        if (f < D) {
-          const float b = __ldg(P + o_bh0 + f);
+        const float b = f < D ? __ldg(P + o_bh0 + f) : 0.f;
+#pragma unroll 1
+        for (int gi = 0; gi < NG; ++gi) {
+          float v[8];
+          tc::tmem_ld8(tq + (uint32_t)(g * CT + 8 * gi), v);
+          if (f < D) {
 #pragma unroll
-          for (int n = 0; n < CT; ++n) tc::store_operand<KIND>(bbuf, n, f, CT, fmaxf(v[n] + b, 0.f));
+            for (int j = 0; j < 8; ++j) tc::store_operand<KIND>(bbuf, 8 * gi + j, f, CT, fmaxf(v[j] + b, 0.f));
+          }
         }
       }
       arrive_act();
+      mark(PF_HEAD1);
       if (!(ok = wait_mma())) break;
+      mark(PF_W_H2);
       // ---- head.2: logits -> scratch
       if (g < 2) {
-        float v[16];
-        tc::tmem_ld16(tq + (uint32_t)(g * CT), v);
         const int vv = g * 128 + row;
         const float b = __ldg(P + o_bh2 + vv);
+#pragma unroll 1
+        for (int gi = 0; gi < NG; ++gi) {
+          float v[8];
+          tc::tmem_ld8(tq + (uint32_t)(g * CT + 8 * gi), v);
 #pragma unroll
-        for (int n = 0; n < CT; ++n) scr[n * 256 + vv] = v[n] + b;
+          for (int j = 0; j < 8; ++j) scr[(8 * gi + j) * 256 + vv] = v[j] + b;
+        }
       }
       cbar_sync();
+      mark(PF_HEAD2);
       // ---- quantiser + range coder, a warp per chunk
       for (int n = cw; n < CT; n += 16) {
         const int c = c0 + n;
-        if (!is_active(n, t)) continue;
+        if (!((amask >> n) & 1u)) continue;
         if (mode == MODE_LOGITS) {
           float* dst = a.logits + ((long long)c * a.n_steps + s) * V;
           for (int v = lane; v < V; v += 32) dst[v] = scr[n * 256 + v];
@@ -600,7 +749,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         }
       }
       cbar_sync();
+      mark(PF_CODER);
     }
+#ifdef BOA_PHASE_PROFILE
+    if (pon) for (int i = 0; i < 20; ++i) a.prof[i] = pacc[i];
+#endif
     if (ok && mode == MODE_ENCODE && ct < CT) {
       const int c = c0 + ct;
       if (c < a.n_chunks) {
@@ -613,7 +766,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   // ------------------------------ teardown ------------------------------
   tc::tc_fence_before();
   __syncthreads();
-  if (tid == 0 && *abort_flag) atomicOr(a.err, RC_ERR_TIMEOUT);
+  if (tid == 0 && *abort_flag) {
+    atomicOr(a.err, RC_ERR_TIMEOUT);
+    // weight copies issued but never consumed must land before the CTA exits
+    for (long long j = *cons_sh; j < *prod_it_sh; ++j) {
+      const int sj = (int)(j % kStagesK);
+      const uint32_t pj = (uint32_t)((j / kStagesK) & 1);
+      const long long t0 = clock64();
+      while (!tc::mbar_try_wait(&full[sj], pj)) {
+        if (clock64() - t0 > kWaitBudget) break;
+      }
+    }
+  }
+  __syncthreads();
   if (warp == 1) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
@@ -738,6 +903,7 @@ using namespace boa;
 
 struct boa_model {
   int D, L, V, kind, device;
+  int n_sms = 148;
   TilePlan plan;
   uint8_t* d_tiles = nullptr;
   float* d_params = nullptr;
@@ -814,17 +980,33 @@ int build_model(boa_model* m, const float* flat, size_t n_floats, std::vector<ui
 size_t conv_state_bytes(const boa_model* m, int n) { return (size_t)n * m->L * (2 * m->D) * 16; }
 size_t ssm_state_bytes(const boa_model* m, int n) { return (size_t)n * m->L * (2 * m->D) * 64; }
 
-template <int D, int KIND>
-int launch_step_t(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
-  const int smem = Smem<D, KIND>::ALLOC;
-  BOA_CUDA(cudaFuncSetAttribute(k_boa_step<D, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  const int grid = cdiv(n_chunks, kCT);
-  k_boa_step<D, KIND><<<grid, kThreads, smem, s>>>(a);
+template <int D, int KIND, int CT>
+int launch_step_ct(StepArgs& a, int n_chunks, cudaStream_t s) {
+  const int smem = Smem<D, KIND, CT>::ALLOC;
+  BOA_CUDA(cudaFuncSetAttribute(k_boa_step<D, KIND, CT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int grid = cdiv(n_chunks, CT);
+  k_boa_step<D, KIND, CT><<<grid, kThreads, smem, s>>>(a);
   BOA_CUDA(cudaGetLastError());
   return BOA_OK;
 }
 
+template <int D, int KIND>
+int launch_step_t(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
+  if constexpr (ChunkTileMax<D, KIND>::value == 32) {
+    // 32 chunks per CTA only when that still fills every SM
+    if (n_chunks >= 32 * m->n_sms) return launch_step_ct<D, KIND, 32>(a, n_chunks, s);
+  }
+  return launch_step_ct<D, KIND, 16>(a, n_chunks, s);
+}
+
+// BOA_PHASE_PROFILE=1: time the phases of CTA 0 and print them (SM cycles) to stderr.
+int launch_step_profiled(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s);
+
 int launch_step(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
+#ifdef BOA_PHASE_PROFILE
+  const char* pe = getenv("BOA_PHASE_PROFILE");
+  if (pe && pe[0] == '1' && a.prof == nullptr) return launch_step_profiled(m, a, n_chunks, s);
+#endif
   a.n_layers = m->L;
   a.vocab = m->V;
   a.tiles_per_step = m->plan.per_step;
@@ -842,6 +1024,30 @@ int launch_step(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
   BOA_DISPATCH(512)
 #undef BOA_DISPATCH
   return boa_fail(BOA_ERR_UNSUPPORTED, "d_model must be 64, 256 or 512");
+}
+
+int launch_step_profiled(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
+  unsigned long long* d = nullptr;
+  BOA_CUDA(cudaMalloc(&d, PF_SLOTS * sizeof(unsigned long long)));
+  BOA_CUDA(cudaMemsetAsync(d, 0, PF_SLOTS * sizeof(unsigned long long), s));
+  a.prof = d;
+  int rc = launch_step(m, a, n_chunks, s);
+  unsigned long long h[PF_SLOTS] = {0};
+  if (rc == BOA_OK) {
+    cudaMemcpyAsync(h, d, sizeof(h), cudaMemcpyDeviceToHost, s);
+    cudaStreamSynchronize(s);
+    static const char* names[20] = {"embed", "ln1", "wait_in", "conv", "wait_xp", "xp_epi", "wait_dt", "scan",
+                                    "wait_out", "out_ln2", "wait_ff1", "ff1_epi", "wait_ff2", "ff2_epi", "head0_in",
+                                    "wait_h0", "head0_epi", "wait_h2", "head2_epi", "coder"};
+    fprintf(stderr, "{\"boa_phase_profile\": {\"mode\": %d, \"steps\": %llu, \"tiles\": %llu", a.mode, h[PF_STEPS],
+            h[PF_TILES]);
+    for (int i = 0; i < 20; ++i) fprintf(stderr, ", \"%s\": %llu", names[i], h[i]);
+    fprintf(stderr, ", \"mma_wait_full\": %llu, \"mma_wait_act\": %llu, \"mma_total\": %llu, \"prod_wait_empty\": %llu}}\n",
+            h[PF_MMA_WAIT_FULL], h[PF_MMA_WAIT_ACT], h[PF_MMA_TOTAL], h[PF_PROD_WAIT_EMPTY]);
+  }
+  cudaFree(d);
+  a.prof = nullptr;
+  return rc;
 }
 
 int check_err(const boa_model* m, cudaStream_t s) {
@@ -886,6 +1092,7 @@ BOA_API int boa_model_create(boa_model** out, int d_model, int n_layers, int voc
   boa_model* m = new boa_model();
   m->D = d_model; m->L = n_layers; m->V = vocab; m->kind = weight_format; m->device = device;
   m->plan = make_plan(d_model, n_layers, weight_format);
+  cudaDeviceGetAttribute(&m->n_sms, cudaDevAttrMultiProcessorCount, device);
   std::vector<uint8_t> tiles;
   std::vector<float> params;
   int rc = BOA_ERR_UNSUPPORTED;
@@ -918,8 +1125,8 @@ BOA_API int boa_model_destroy(boa_model* m) {
 
 BOA_API size_t boa_model_workspace_bytes(const boa_model* m, int n_chunks) {
   if (!m || n_chunks < 1) return 0;
-  // state is addressed per CTA tile of 16 chunks, so round the count up
-  const int n = cdiv(n_chunks, kCT) * kCT;
+  // state is addressed per CTA tile of up to 32 chunks, so round the count up
+  const int n = cdiv(n_chunks, 32) * 32;
   return conv_state_bytes(m, n) + ssm_state_bytes(m, n);
 }
 
