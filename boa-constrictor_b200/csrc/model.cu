@@ -66,21 +66,23 @@ struct LayerParams {
 
 static inline int cdiv(int a, int b) { return (a + b - 1) / b; }
 
-// Projection tile counts per step (must match the kernel's consumption order).
+// Projection tile counts per step for one CTA of a `split`-way cluster (must
+// match the kernel's consumption order; every rank streams the same count).
 struct TilePlan {
   int per, kD, kE, kF, mtE, mtD, mtF;
-  int t_in, t_xp, t_dt, t_out, t_ff1, t_ff2, t_h0, t_h2, per_layer, per_step;
+  int split, ltE, ltD, ltF, ltV;
+  int per_layer, per_step;
 };
-static TilePlan make_plan(int D, int L, int kind) {
+static TilePlan make_plan(int D, int L, int kind, int split) {
   TilePlan p{};
   p.per = kind == 0 ? 32 : 64;
   const int E = 2 * D, F = 4 * D;
   p.kD = D / p.per; p.kE = E / p.per; p.kF = F / p.per;
   p.mtE = E / 128; p.mtD = cdiv(D, 128); p.mtF = F / 128;
-  p.t_in = 2 * p.mtE * p.kD; p.t_xp = p.kE; p.t_dt = p.mtE; p.t_out = p.mtD * p.kE;
-  p.t_ff1 = p.mtF * p.kD; p.t_ff2 = p.mtD * p.kF; p.t_h0 = p.mtD * p.kD; p.t_h2 = 2 * p.kD;
-  p.per_layer = p.t_in + p.t_xp + p.t_dt + p.t_out + p.t_ff1 + p.t_ff2;
-  p.per_step = p.per_layer * L + p.t_h0 + p.t_h2;
+  p.split = split;
+  p.ltE = p.mtE / split; p.ltD = p.mtD / split; p.ltF = p.mtF / split; p.ltV = 2 / split;
+  p.per_layer = 2 * p.ltE * p.kD + p.kE + p.ltE + p.ltD * p.kE + p.ltF * p.kD + p.ltD * p.kF;
+  p.per_step = p.per_layer * L + p.ltD * p.kD + p.ltV * p.kD;
   return p;
 }
 
@@ -136,31 +138,35 @@ struct ChunkTileMax {
   static constexpr int value = (KIND != 0 && D <= 256) ? 32 : 16;
 };
 
-// Shared-memory carve-up (dynamic smem, base rounded up to 1024 bytes).  The
-// fp32 scratch (LN2 input / logits) lives in the upper part of the operand
-// buffer when it fits: whenever it is written, the operand there (the
-// out_proj input y or the head.2 input) has already been consumed.
-template <int D, int KIND, int CT_>
+// Shared-memory carve-up (dynamic smem, base rounded up to 1024 bytes).
+//   SPLIT == 1: one operand buffer; the fp32 scratch (LN2 input / logits)
+//               aliases its upper part when it fits (the operand there has
+//               been consumed whenever the scratch is written).
+//   SPLIT == 2: two operand buffers used alternately by consecutive GEMMs, so
+//               the peer CTA can write the next operand while this CTA's
+//               tensor core may still read the current one; separate scratch.
+template <int D, int KIND, int CT_, int SPLIT>
 struct Smem {
   static constexpr int CT = CT_;
   static constexpr int EB = tc::OpKind<KIND>::kElemBytes;
   static constexpr int E = 2 * D, F = 4 * D;
   static constexpr int BBUF = CT * F * EB;                  // largest K is F
+  static constexpr int NBUF = SPLIT;
   static constexpr int Y_BYTES = CT * E * EB;               // out_proj input (also covers LN2 / head inputs)
   static constexpr int SCR = CT * (D > 256 ? D : 256) * 4;  // LN2 input / logits (fp32)
-  static constexpr bool SCR_ALIAS = BBUF - Y_BYTES >= SCR;
+  static constexpr bool SCR_ALIAS = SPLIT == 1 && BBUF - Y_BYTES >= SCR;
   static constexpr int HRES = CT * D * 4;
   static constexpr int DBCB = CT * 64 * 4;
   static constexpr int o_bbuf = 0;
-  static constexpr int o_scr = SCR_ALIAS ? Y_BYTES : BBUF;
-  static constexpr int o_hres = SCR_ALIAS ? BBUF : BBUF + SCR;
+  static constexpr int o_scr = SCR_ALIAS ? Y_BYTES : NBUF * BBUF;
+  static constexpr int o_hres = SCR_ALIAS ? BBUF : NBUF * BBUF + SCR;
   static constexpr int o_dbc = o_hres + HRES;
   static constexpr int o_enc = o_dbc + DBCB;                 // RcEnc / RcDec [CT]
   static constexpr int o_prev = o_enc + CT * 32;
   static constexpr int o_lens = o_prev + CT * 4;
   static constexpr int o_bars = o_lens + CT * 4;
   static constexpr int kMaxStages = 12;
-  static constexpr int o_misc = o_bars + (2 * kMaxStages + 3) * 8;
+  static constexpr int o_misc = o_bars + (2 * kMaxStages + 4) * 8;
   static constexpr int o_prof = o_misc + 64;                 // PF_SLOTS x u64 phase accumulators
   static constexpr int o_ring = ((o_prof + 256 + 1023) / 1024) * 1024;
   static constexpr int kBudget = 227 * 1024 - 1024;          // minus alignment slack
@@ -178,10 +184,68 @@ __device__ __forceinline__ float ex2_approx(float x) {
 }
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
+// ----------------------------- cluster helpers ------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory byte in CTA `peer` of this cluster.
+__device__ __forceinline__ uint32_t peer_addr(const void* local, uint32_t peer) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(tc::smem_u32(local)), "r"(peer));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_b16(uint32_t addr, unsigned short v) {
+  asm volatile("st.shared::cluster.b16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_b32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(tc::smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  long long budget) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > budget) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_cluster() {
+  asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
+}
+
 // -------------------------------- the kernel --------------------------------
-template <int D, int KIND, int CT_>
+// SPLIT == 2 runs as clusters of two CTAs over the same chunk tile: CTA r
+// computes output features / channels [r/2, (r+1)/2) of every projection
+// (x_proj, whose output is tiny, runs whole in both), streams only its half of
+// the weights, and writes every value the peer needs into the peer's shared
+// memory as well (DSMEM).  LayerNorms and the coder run redundantly in both
+// CTAs on identical data; CTA 0 writes the codec outputs.
+template <int D, int KIND, int CT_, int SPLIT>
 __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant__ StepArgs a) {
-  using S = Smem<D, KIND, CT_>;
+  using S = Smem<D, KIND, CT_, SPLIT>;
   using LP = LayerParams<D>;
   constexpr int CT = S::CT;
   constexpr int NG = CT / 8;                             // groups of 8 chunks
@@ -190,16 +254,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   constexpr int PER = 128 / tc::OpKind<KIND>::kElemBytes;
   constexpr int kD = D / PER, kE = E / PER, kF = F / PER;
   constexpr int MT_E = E / 128, MT_D = (D + 127) / 128, MT_F = F / 128;
-  constexpr int COL_X = 0, COL_Z = MT_E * CT, COL_XP = 2 * MT_E * CT, COL_DT = COL_XP + CT;
-  static_assert(COL_DT + MT_E * CT <= 512, "TMEM budget");
-  static_assert(MT_F * CT <= 512, "TMEM budget (ff.0)");
+  // tiles owned by this CTA
+  constexpr int LT_E = MT_E / SPLIT, LT_D = MT_D / SPLIT, LT_F = MT_F / SPLIT, LT_V = 2 / SPLIT;
+  static_assert(SPLIT == 1 || (MT_E % 2 == 0 && MT_D % 2 == 0), "split needs an even number of tiles");
+  constexpr int COL_X = 0, COL_Z = LT_E * CT, COL_XP = 2 * LT_E * CT, COL_DT = COL_XP + CT;
+  static_assert(COL_DT + LT_E * CT <= 512, "TMEM budget");
+  static_assert(LT_F * CT <= 512, "TMEM budget (ff.0)");
   static_assert(R <= PER && DBC <= 64, "x_proj outputs must fit one tile / one K slice");
   static_assert(D % 32 == 0 && D >= 64, "d_model");
+  // per-channel phases: (tile, chunk run) units spread over the 4 warp groups
+  constexpr int RUNS = LT_E >= 4 ? 1 : 4 / LT_E;         // chunk runs per local channel tile
+  constexpr int RUN = CT / RUNS;
+  static_assert(RUN % 4 == 0 && RUN >= 4, "chunk run");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem + S::o_ring;
-  uint8_t* bbuf = smem + S::o_bbuf;
+  uint8_t* bbuf0 = smem + S::o_bbuf;
   float* hres = reinterpret_cast<float*>(smem + S::o_hres);
   float* scr = reinterpret_cast<float*>(smem + S::o_scr);
   float* dbc = reinterpret_cast<float*>(smem + S::o_dbc);
@@ -210,6 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   uint64_t* mma_bar = empty + S::kMaxStages;
   uint64_t* act_bar = mma_bar + 1;
   uint64_t* drain_bar = act_bar + 1;
+  uint64_t* xch_bar = drain_bar + 1;                      // peer finished writing an exchange
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::o_misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::o_misc + 4);
   int* nsteps_sh = reinterpret_cast<int*>(smem + S::o_misc + 8);
@@ -219,7 +291,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int c0 = blockIdx.x * CT;
+  const uint32_t rank = SPLIT == 2 ? cluster_rank() : 0u;
+  const uint32_t peer = rank ^ 1u;
+  const int c0 = (blockIdx.x / SPLIT) * CT;
   const int mode = a.mode;
   const int L = a.n_layers;
   const int V = a.vocab;
@@ -227,13 +301,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   const long long o_bh0 = (long long)LP::stride * L;
   const long long o_bh2 = o_bh0 + D;
   const long long o_emb = o_bh2 + 256;
+  const bool writer = rank == 0;                          // writes the codec outputs
 
   // ------------------------------- setup -------------------------------
   if (tid == 0) {
     for (int s = 0; s < kStagesK; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
     tc::mbar_init(mma_bar, 1);
-    tc::mbar_init(act_bar, kComputeThreads);
+    tc::mbar_init(act_bar, kComputeThreads * SPLIT);      // both CTAs' compute threads
     tc::mbar_init(drain_bar, 1);
+    tc::mbar_init(xch_bar, kComputeThreads);              // the peer's compute threads
     *abort_flag = 0;
     *cons_sh = 0;
     *prod_it_sh = 0;
@@ -268,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         int nw = a.sizes_in[c];
         nw = nw < 0 ? 0 : (nw > a.pitch_words ? a.pitch_words : nw);
         rc_dec_reset(reinterpret_cast<RcDec*>(smem + S::o_enc)[n], a.words_in + (long long)c * a.pitch_words, nw);
-        a.out[(long long)c * a.out_pitch] = (uint8_t)p0;
+        if (writer) a.out[(long long)c * a.out_pitch] = (uint8_t)p0;
       } else {
         len = 0x7fffffff;
         p0 = a.tokens[(long long)c * a.n_steps];
@@ -279,6 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   }
   tc::tc_fence_before();
   __syncthreads();
+  if constexpr (SPLIT == 2) cluster_sync_all();           // peer barriers initialised before any remote arrive
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int nsteps = *nsteps_sh;
@@ -291,14 +368,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       int st = 0;
       uint32_t ph = 0;
       bool ok = true;
-      #ifdef BOA_PHASE_PROFILE
+#ifdef BOA_PHASE_PROFILE
       const bool prof = a.prof != nullptr && blockIdx.x == 0;
 #else
       constexpr bool prof = false;
 #endif
       unsigned long long w_empty = 0;
+      const uint8_t* base = a.wtiles + (long long)rank * a.tiles_per_step * kTileBytes;
       for (int s = 0; s < nsteps && ok; ++s) {
-        const uint8_t* src = a.wtiles;
+        const uint8_t* src = base;
         for (int t = 0; t < a.tiles_per_step; ++t, ++it, src += kTileBytes) {
           const long long tw = prof ? clock64() : 0;
           if (!tc::mbar_wait(&empty[st], ph ^ 1u, abort_flag, kWaitBudget)) { ok = false; break; }
@@ -316,15 +394,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
     if (lane == 0 && nsteps > 0) {
       const uint32_t id = tc::idesc<KIND>(128, CT);
       const uint64_t adesc0 = tc::sdesc_sw128(tc::smem_u32(ring));
-      const uint64_t bdesc0 = tc::sdesc_sw128(tc::smem_u32(bbuf));
       constexpr uint64_t kTileDesc = kTileBytes >> 4;      // descriptor start-address units (16 B)
       constexpr uint64_t kSliceDesc = (CT * 128) >> 4;
+      constexpr uint64_t kBufDesc = S::BBUF >> 4;
+      const uint64_t bdesc_base = tc::sdesc_sw128(tc::smem_u32(bbuf0));
       long long it = 0;
       int st = 0;
       uint32_t ph = 0;
       uint32_t act_phase = 0;
+      int gemm_no = 0;                                     // selects the operand buffer
       bool ok = true;
-      #ifdef BOA_PHASE_PROFILE
+#ifdef BOA_PHASE_PROFILE
       const bool prof = a.prof != nullptr && blockIdx.x == 0;
 #else
       constexpr bool prof = false;
@@ -333,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       const long long t_mma0 = clock64();
       // D[col0 + mt*CT ...] = sum over ks of A(mt, ks) * B(ks)^T
       auto gemm = [&](int n_mt, int n_ks, int col0) -> bool {
+        const uint64_t bdesc0 = bdesc_base + (uint64_t)(gemm_no % S::NBUF) * kBufDesc;
         uint32_t dcol = tmem + (uint32_t)col0;
         for (int mt = 0; mt < n_mt; ++mt, dcol += CT) {
           uint64_t bd = bdesc0;
@@ -355,25 +436,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       };
       auto step_gemm = [&](int n_mt, int n_ks, int col0) -> bool {
         const long long tw = prof ? clock64() : 0;
-        if (!tc::mbar_wait(act_bar, act_phase, abort_flag, kWaitBudget)) return false;
+        const bool got = SPLIT == 2 ? mbar_wait_cluster(act_bar, act_phase, abort_flag, kWaitBudget)
+                                    : tc::mbar_wait(act_bar, act_phase, abort_flag, kWaitBudget);
+        if (!got) return false;
         if (prof) w_act += clock64() - tw;
         act_phase ^= 1u;
         tc::tc_fence_after();
         if (!gemm(n_mt, n_ks, col0)) return false;
         tc::mma_commit(mma_bar);
+        ++gemm_no;
         return true;
       };
       for (int s = 0; s < nsteps && ok; ++s) {
         for (int l = 0; l < L && ok; ++l) {
-          ok = step_gemm(2 * MT_E, kD, 0)          // in_proj -> x | z
-               && step_gemm(1, kE, COL_XP)         // x_proj
-               && step_gemm(MT_E, 1, COL_DT)       // dt_proj
-               && step_gemm(MT_D, kE, 0)           // out_proj
-               && step_gemm(MT_F, kD, 0)           // ff.0
-               && step_gemm(MT_D, kF, 0);          // ff.2
+          ok = step_gemm(2 * LT_E, kD, 0)          // in_proj -> x | z (own channels)
+               && step_gemm(1, kE, COL_XP)         // x_proj (whole)
+               && step_gemm(LT_E, 1, COL_DT)       // dt_proj (own channels)
+               && step_gemm(LT_D, kE, 0)           // out_proj (own features)
+               && step_gemm(LT_F, kD, 0)           // ff.0
+               && step_gemm(LT_D, kF, 0);          // ff.2
         }
-        ok = ok && step_gemm(MT_D, kD, 0)          // head.0
-             && step_gemm(2, kD, 0);               // head.2
+        ok = ok && step_gemm(LT_D, kD, 0)          // head.0
+             && step_gemm(LT_V, kD, 0);            // head.2
       }
       if (prof) {
         a.prof[PF_MMA_WAIT_FULL] = w_full;
@@ -397,9 +481,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
     const int g = cw >> 2;                   // group 0..3 (covers all four quarters)
     const int row = 32 * q + lane;           // row inside a 128-row M tile
     const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
-    uint32_t mma_phase = 0;
+    uint32_t mma_phase = 0, xch_phase = 0;
+    int gemm_no = 0;                         // operand buffer of the next GEMM = gemm_no % NBUF
     RcEnc* encs = reinterpret_cast<RcEnc*>(smem + S::o_enc);
     RcDec* decs = reinterpret_cast<RcDec*>(smem + S::o_enc);
+    const uint32_t peer_bbuf = SPLIT == 2 ? peer_addr(bbuf0, peer) : 0u;
+    const uint32_t peer_hres = SPLIT == 2 ? peer_addr(hres, peer) : 0u;
+    const uint32_t peer_scr = SPLIT == 2 ? peer_addr(scr, peer) : 0u;
+    const uint32_t peer_act = SPLIT == 2 ? peer_addr(act_bar, peer) : 0u;
+    const uint32_t peer_xch = SPLIT == 2 ? peer_addr(xch_bar, peer) : 0u;
 #ifdef BOA_PHASE_PROFILE
     const bool pon = a.prof != nullptr && blockIdx.x == 0 && ct == 0;
     unsigned long long* pacc = reinterpret_cast<unsigned long long*>(smem + S::o_prof);
@@ -411,11 +501,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
 #else
     auto mark = [](int) {};
 #endif
-
+    // operand buffer the next GEMM reads
+    auto bnext = [&]() -> uint8_t* { return bbuf0 + (gemm_no % S::NBUF) * S::BBUF; };
+    // write one operand element of the next GEMM, also into the peer when `share`
+    auto put_b = [&](uint8_t* buf, int n, int k, float v, bool share) {
+      const uint32_t off = tc::sw128_offset<KIND>(n, k, CT);
+      tc::store_operand<KIND>(buf, n, k, CT, v);
+      if constexpr (SPLIT == 2) {
+        if (share) {
+          const uint32_t raddr = peer_bbuf + (uint32_t)(buf - bbuf0) + off;
+          if constexpr (KIND == 0) {
+            st_cluster_b32(raddr, *reinterpret_cast<const uint32_t*>(buf + off));
+          } else {
+            st_cluster_b16(raddr, *reinterpret_cast<const unsigned short*>(buf + off));
+          }
+        }
+      }
+    };
+    auto put_f32 = [&](float* arr, uint32_t peer_arr, int idx, float v) {
+      arr[idx] = v;
+      if constexpr (SPLIT == 2) st_cluster_b32(peer_arr + 4u * (uint32_t)idx, __float_as_uint(v));
+    };
     auto arrive_act = [&]() {
-      tc::fence_proxy_async_smem();
+      if constexpr (SPLIT == 2) fence_proxy_async_cluster();
+      else tc::fence_proxy_async_smem();
       tc::tc_fence_before();
       tc::mbar_arrive(act_bar);
+      if constexpr (SPLIT == 2) mbar_arrive_remote(peer_act);
+      ++gemm_no;
     };
     // Wait for the GEMM just issued; the verdict is uniform over the 512 threads.
     auto wait_mma = [&]() -> bool {
@@ -425,28 +538,40 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       tc::tc_fence_after();
       return *abort_flag == 0;
     };
+    // After writing shared values into the peer: tell it, then wait for its
+    // values to have arrived here.  Uniform verdict as wait_mma.
+    auto exchange = [&]() -> bool {
+      if constexpr (SPLIT == 2) {
+        mbar_arrive_remote(peer_xch);
+        mbar_wait_cluster(xch_bar, xch_phase, abort_flag, kWaitBudget);
+        xch_phase ^= 1u;
+      }
+      cbar_sync();
+      return *abort_flag == 0;
+    };
     // LayerNorm (eps 1e-5, biased variance, two passes) of CT rows of `src`
-    // (fp32 [CT][D]) into the B operand; a warp per chunk.
+    // (fp32 [CT][D]) into the next operand; a warp per chunk, whole rows.
     auto layernorm_to_b = [&](const float* src, const float* w, const float* b) {
-      constexpr int PL = D / 32;
+      constexpr int PLN = D / 32;
+      uint8_t* buf = bnext();
       for (int n = cw; n < CT; n += 16) {
-        float v[PL];
+        float v[PLN];
         float s = 0.f;
 #pragma unroll
-        for (int i = 0; i < PL; ++i) { v[i] = src[n * D + lane + 32 * i]; s += v[i]; }
+        for (int i = 0; i < PLN; ++i) { v[i] = src[n * D + lane + 32 * i]; s += v[i]; }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
         const float mean = s * (1.0f / D);
         float var = 0.f;
 #pragma unroll
-        for (int i = 0; i < PL; ++i) { const float dl = v[i] - mean; var += dl * dl; }
+        for (int i = 0; i < PLN; ++i) { const float dl = v[i] - mean; var += dl * dl; }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
         const float rstd = rsqrtf(var * (1.0f / D) + 1e-5f);
 #pragma unroll
-        for (int i = 0; i < PL; ++i) {
+        for (int i = 0; i < PLN; ++i) {
           const int f = lane + 32 * i;
-          tc::store_operand<KIND>(bbuf, n, f, CT, (v[i] - mean) * rstd * __ldg(w + f) + __ldg(b + f));
+          tc::store_operand<KIND>(buf, n, f, CT, (v[i] - mean) * rstd * __ldg(w + f) + __ldg(b + f));
         }
       }
     };
@@ -460,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
 #pragma unroll
       for (int n = 0; n < CT; ++n) amask |= (t < lens_sh[n] ? 1u : 0u) << n;
       const uint32_t lmask = load_state ? amask : 0u;
-      // ---- embedding
+      // ---- embedding (both CTAs, whole rows)
       for (int i = ct; i < CT * D; i += kComputeThreads) {
         const int n = i / D, f = i - (i / D) * D;
         hres[i] = __ldg(P + o_emb + (long long)prev[n] * D + f);
@@ -469,52 +594,47 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       mark(PF_EMBED);
       for (int l = 0; l < L && ok; ++l) {
         const float* lp = P + (long long)LP::stride * l;
-        // ---- LN1 -> B ; in_proj
+        // ---- LN1 -> operand ; in_proj
         layernorm_to_b(hres, lp + LP::ln1w, lp + LP::ln1b);
         arrive_act();
         mark(PF_LN1);
         if (!(ok = wait_mma())) break;
         mark(PF_W_IN);
-        // ---- causal conv (width 4) + SiLU, thread per channel; xc -> B and TMEM.
-        //      The next 8 chunks' windows load while the current 8 compute.
-        for (int mt = g; mt < MT_E; mt += 4) {
-          const int e = mt * 128 + row;
-          const float4 w = __ldg(reinterpret_cast<const float4*>(lp + LP::convw) + e);
-          const float cb = __ldg(lp + LP::convb + e);
-          float4* cs = a.conv_state + ((long long)c0 * L + l) * E + e;   // chunk stride L*E
-          const long long cst = (long long)L * E;
-          float4 nx[8];
+        // ---- causal conv (width 4) + SiLU, thread per own channel; xc -> both
+        //      CTAs' operand (x_proj runs whole) and into TMEM for the scan
+        {
+          uint8_t* buf = bnext();
+          for (int u = g; u < LT_E * NG; u += 4) {
+            const int lt = u / NG;
+            const int e = (int)(rank * LT_E + lt) * 128 + row;
+            const float4 w = __ldg(reinterpret_cast<const float4*>(lp + LP::convw) + e);
+            const float cb = __ldg(lp + LP::convb + e);
+            float4* cs = a.conv_state + ((long long)c0 * L + l) * E + e;   // chunk stride L*E
+            const long long cst = (long long)L * E;
+            {
+              const int nb = (u % NG) * 8;
+              float4 stv[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) nx[j] = ((lmask >> j) & 1u) ? cs[j * cst] : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 1
-          for (int gi = 0; gi < NG; ++gi) {
-            float4 st[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) st[j] = nx[j];
-            if (gi + 1 < NG) {
+              for (int j = 0; j < 8; ++j)
+                stv[j] = ((lmask >> (nb + j)) & 1u) ? cs[(nb + j) * cst] : make_float4(0.f, 0.f, 0.f, 0.f);
+              float xv[8];
+              const uint32_t col = (uint32_t)(COL_X + lt * CT + nb);
+              tc::tmem_ld8(tq + col, xv);
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                const int n = 8 * (gi + 1) + j;
-                nx[j] = ((lmask >> n) & 1u) ? cs[n * cst] : make_float4(0.f, 0.f, 0.f, 0.f);
+                const int n = nb + j;
+                float acc = cb;
+                acc = fmaf(w.x, stv[j].x, acc);
+                acc = fmaf(w.y, stv[j].y, acc);
+                acc = fmaf(w.z, stv[j].z, acc);
+                acc = fmaf(w.w, xv[j], acc);
+                const float xc = silu_fast(acc);
+                if ((amask >> n) & 1u) cs[n * cst] = make_float4(stv[j].y, stv[j].z, xv[j], 0.f);
+                put_b(buf, n, e, xc, true);
+                xv[j] = xc;
               }
+              tc::tmem_st8(tq + col, xv);
             }
-            float xv[8];
-            const uint32_t col = (uint32_t)(COL_X + mt * CT + 8 * gi);
-            tc::tmem_ld8(tq + col, xv);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int n = 8 * gi + j;
-              float acc = cb;
-              acc = fmaf(w.x, st[j].x, acc);
-              acc = fmaf(w.y, st[j].y, acc);
-              acc = fmaf(w.z, st[j].z, acc);
-              acc = fmaf(w.w, xv[j], acc);
-              const float xc = silu_fast(acc);
-              if ((amask >> n) & 1u) cs[n * cst] = make_float4(st[j].y, st[j].z, xv[j], 0.f);
-              tc::store_operand<KIND>(bbuf, n, e, CT, xc);
-              xv[j] = xc;
-            }
-            tc::tmem_st8(tq + col, xv);
           }
           tc::tmem_wait_st();
         }
@@ -522,19 +642,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         mark(PF_CONV);
         if (!(ok = wait_mma())) break;
         mark(PF_W_XP);
-        // ---- x_proj epilogue: dt_r -> B (K slice 0, zero padded), B/C -> smem
-        if (g == 0) {
+        // ---- x_proj epilogue: dt_r -> operand (K slice 0, zero padded), B/C -> smem
+        {
+          uint8_t* buf = bnext();
+          if (g == 0) {
 #pragma unroll 1
-          for (int gi = 0; gi < NG; ++gi) {
-            float v[8];
-            tc::tmem_ld8(tq + (uint32_t)(COL_XP + 8 * gi), v);
-            if (row < DBC) {
+            for (int gi = 0; gi < NG; ++gi) {
+              float v[8];
+              tc::tmem_ld8(tq + (uint32_t)(COL_XP + 8 * gi), v);
+              if (row < DBC) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) dbc[(8 * gi + j) * 64 + row] = v[j];
-            }
-            if (row < PER) {
+                for (int j = 0; j < 8; ++j) dbc[(8 * gi + j) * 64 + row] = v[j];
+              }
+              if (row < PER) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) tc::store_operand<KIND>(bbuf, 8 * gi + j, row, CT, row < R ? v[j] : 0.f);
+                for (int j = 0; j < 8; ++j) tc::store_operand<KIND>(buf, 8 * gi + j, row, CT, row < R ? v[j] : 0.f);
+              }
             }
           }
         }
@@ -542,64 +665,69 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         mark(PF_XP);
         if (!(ok = wait_mma())) break;
         mark(PF_W_DT);
-        // ---- selective scan + D skip + SiLU(z) gate, thread per channel; the
-        //      next chunk's state loads while the current one computes, and
-        //      A*log2(e) is re-read from L1 per chunk to keep registers free
-        for (int mt = g; mt < MT_E; mt += 4) {
-          const int e = mt * 128 + row;
-          const float4* A2p = reinterpret_cast<const float4*>(lp + LP::A2) + e * 4;
-          const float Dp = __ldg(lp + LP::Dp + e);
-          const float bdt = __ldg(lp + LP::dtb + e);
-          float4* ss = a.ssm_state + (((long long)c0 * L + l) * E + e) * 4;   // chunk stride L*E*4
-          const long long cstride = (long long)L * E * 4;
-          float4 nx[4];
+        // ---- selective scan + D skip + SiLU(z) gate, thread per own channel
+        //      and chunk run; the next chunk's state loads while one computes
+        {
+          uint8_t* buf = bnext();
+          for (int u = g; u < LT_E * RUNS; u += 4) {
+            const int lt = u / RUNS, n0 = (u % RUNS) * RUN;
+            const int e = (int)(rank * LT_E + lt) * 128 + row;
+            const float4* A2p = reinterpret_cast<const float4*>(lp + LP::A2) + e * 4;
+            const float Dp = __ldg(lp + LP::Dp + e);
+            const float bdt = __ldg(lp + LP::dtb + e);
+            float4* ss = a.ssm_state + (((long long)c0 * L + l) * E + e) * 4;   // chunk stride L*E*4
+            const long long cstride = (long long)L * E * 4;
+            float4 nx[4];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) nx[k] = (lmask & 1u) ? ss[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int k = 0; k < 4; ++k)
+              nx[k] = ((lmask >> n0) & 1u) ? ss[n0 * cstride + k] : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-          for (int gi = 0; gi < CT / 4; ++gi) {
-            float xc[4], z[4], dtr[4];
-            tc::tmem_ld4(tq + (uint32_t)(COL_X + mt * CT + 4 * gi), xc);
-            tc::tmem_ld4(tq + (uint32_t)(COL_Z + mt * CT + 4 * gi), z);
-            tc::tmem_ld4(tq + (uint32_t)(COL_DT + mt * CT + 4 * gi), dtr);
+            for (int gi = 0; gi < RUN / 4; ++gi) {
+              const int nb = n0 + 4 * gi;
+              float xc[4], z[4], dtr[4];
+              tc::tmem_ld4(tq + (uint32_t)(COL_X + lt * CT + nb), xc);
+              tc::tmem_ld4(tq + (uint32_t)(COL_Z + lt * CT + nb), z);
+              tc::tmem_ld4(tq + (uint32_t)(COL_DT + lt * CT + nb), dtr);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int n = 4 * gi + j;
-              float h[16];
+              for (int j = 0; j < 4; ++j) {
+                const int n = nb + j;
+                float h[16];
 #pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                h[4 * k] = nx[k].x; h[4 * k + 1] = nx[k].y; h[4 * k + 2] = nx[k].z; h[4 * k + 3] = nx[k].w;
+                for (int k = 0; k < 4; ++k) {
+                  h[4 * k] = nx[k].x; h[4 * k + 1] = nx[k].y; h[4 * k + 2] = nx[k].z; h[4 * k + 3] = nx[k].w;
+                }
+                if (n + 1 < n0 + RUN) {
+#pragma unroll
+                  for (int k = 0; k < 4; ++k)
+                    nx[k] = ((lmask >> (n + 1)) & 1u) ? ss[(n + 1) * cstride + k] : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                const float dtv = softplus_f(dtr[j] + bdt);
+                const float dx = dtv * xc[j];
+                const float4* bc4 = reinterpret_cast<const float4*>(dbc + n * 64 + R);
+                float y = 0.f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const float4 A4 = __ldg(A2p + k);
+                  const float4 B4 = bc4[k];
+                  const float4 C4 = bc4[4 + k];
+                  h[4 * k + 0] = fmaf(h[4 * k + 0], ex2_approx(dtv * A4.x), dx * B4.x);
+                  h[4 * k + 1] = fmaf(h[4 * k + 1], ex2_approx(dtv * A4.y), dx * B4.y);
+                  h[4 * k + 2] = fmaf(h[4 * k + 2], ex2_approx(dtv * A4.z), dx * B4.z);
+                  h[4 * k + 3] = fmaf(h[4 * k + 3], ex2_approx(dtv * A4.w), dx * B4.w);
+                  y = fmaf(h[4 * k + 0], C4.x, y);
+                  y = fmaf(h[4 * k + 1], C4.y, y);
+                  y = fmaf(h[4 * k + 2], C4.z, y);
+                  y = fmaf(h[4 * k + 3], C4.w, y);
+                }
+                if ((amask >> n) & 1u) {
+#pragma unroll
+                  for (int k = 0; k < 4; ++k)
+                    ss[n * cstride + k] = make_float4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
+                }
+                y = fmaf(Dp, xc[j], y);
+                y *= silu_fast(z[j]);
+                put_b(buf, n, e, y, true);
               }
-              if (n + 1 < CT) {
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                  nx[k] = ((lmask >> (n + 1)) & 1u) ? ss[(n + 1) * cstride + k] : make_float4(0.f, 0.f, 0.f, 0.f);
-              }
-              const float dtv = softplus_f(dtr[j] + bdt);
-              const float dx = dtv * xc[j];
-              const float4* bc4 = reinterpret_cast<const float4*>(dbc + n * 64 + R);
-              float y = 0.f;
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float4 A4 = __ldg(A2p + k);
-                const float4 B4 = bc4[k];
-                const float4 C4 = bc4[4 + k];
-                h[4 * k + 0] = fmaf(h[4 * k + 0], ex2_approx(dtv * A4.x), dx * B4.x);
-                h[4 * k + 1] = fmaf(h[4 * k + 1], ex2_approx(dtv * A4.y), dx * B4.y);
-                h[4 * k + 2] = fmaf(h[4 * k + 2], ex2_approx(dtv * A4.z), dx * B4.z);
-                h[4 * k + 3] = fmaf(h[4 * k + 3], ex2_approx(dtv * A4.w), dx * B4.w);
-                y = fmaf(h[4 * k + 0], C4.x, y);
-                y = fmaf(h[4 * k + 1], C4.y, y);
-                y = fmaf(h[4 * k + 2], C4.z, y);
-                y = fmaf(h[4 * k + 3], C4.w, y);
-              }
-              if ((amask >> n) & 1u) {
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                  ss[n * cstride + k] = make_float4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
-              }
-              y = fmaf(Dp, xc[j], y);
-              y *= silu_fast(z[j]);
-              tc::store_operand<KIND>(bbuf, n, e, CT, y);
             }
           }
         }
@@ -607,78 +735,82 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         mark(PF_SCAN);
         if (!(ok = wait_mma())) break;
         mark(PF_W_OUT);
-        // ---- out_proj epilogue -> scratch, then LN2 -> B
-        if (g < MT_D) {
-          const int f = g * 128 + row;
-#pragma unroll 1
-          for (int gi = 0; gi < NG; ++gi) {
-            float v[8];
-            tc::tmem_ld8(tq + (uint32_t)(g * CT + 8 * gi), v);
-            if (f < D) {
+        // ---- out_proj epilogue (own features) -> both CTAs' scratch, then LN2
+        for (int u = g; u < LT_D * NG; u += 4) {
+          const int lt = u / NG, gi = u % NG;
+          const int f = (int)(rank * LT_D + lt) * 128 + row;
+          float v[8];
+          tc::tmem_ld8(tq + (uint32_t)(lt * CT + 8 * gi), v);
+          if (f < D) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) scr[(8 * gi + j) * D + f] = v[j];
-            }
+            for (int j = 0; j < 8; ++j) put_f32(scr, peer_scr, (8 * gi + j) * D + f, v[j]);
           }
         }
-        cbar_sync();
+        if (!(ok = exchange())) break;
         layernorm_to_b(scr, lp + LP::ln2w, lp + LP::ln2b);
         arrive_act();
         mark(PF_LN2);
         if (!(ok = wait_mma())) break;
         mark(PF_W_FF1);
-        // ---- ff.0 epilogue: + b1, exact GELU -> B
-        for (int mt = g; mt < MT_F; mt += 4) {
-          const int f = mt * 128 + row;
-          const float b = __ldg(lp + LP::b1 + f);
-#pragma unroll 1
-          for (int gi = 0; gi < NG; ++gi) {
+        // ---- ff.0 epilogue (own features): + b1, exact GELU -> both operands
+        {
+          uint8_t* buf = bnext();
+          for (int u = g; u < LT_F * NG; u += 4) {
+            const int lt = u / NG, gi = u % NG;
+            const int f = (int)(rank * LT_F + lt) * 128 + row;
+            const float b = __ldg(lp + LP::b1 + f);
             float v[8];
-            tc::tmem_ld8(tq + (uint32_t)(mt * CT + 8 * gi), v);
+            tc::tmem_ld8(tq + (uint32_t)(lt * CT + 8 * gi), v);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) tc::store_operand<KIND>(bbuf, 8 * gi + j, f, CT, gelu_f(v[j] + b));
+            for (int j = 0; j < 8; ++j) put_b(buf, 8 * gi + j, f, gelu_f(v[j] + b), true);
           }
         }
         arrive_act();
         mark(PF_FF1);
         if (!(ok = wait_mma())) break;
         mark(PF_W_FF2);
-        // ---- ff.2 epilogue: residual update
-        if (g < MT_D) {
-          const int f = g * 128 + row;
-          const float b = f < D ? __ldg(lp + LP::b2 + f) : 0.f;
-#pragma unroll 1
-          for (int gi = 0; gi < NG; ++gi) {
-            float v[8];
-            tc::tmem_ld8(tq + (uint32_t)(g * CT + 8 * gi), v);
-            if (f < D) {
+        // ---- ff.2 epilogue (own features): residual update in both CTAs
+        for (int u = g; u < LT_D * NG; u += 4) {
+          const int lt = u / NG, gi = u % NG;
+          const int f = (int)(rank * LT_D + lt) * 128 + row;
+          float v[8];
+          tc::tmem_ld8(tq + (uint32_t)(lt * CT + 8 * gi), v);
+          if (f < D) {
+            const float b = __ldg(lp + LP::b2 + f);
 #pragma unroll
-              for (int j = 0; j < 8; ++j) hres[(8 * gi + j) * D + f] += v[j] + b;
+            for (int j = 0; j < 8; ++j) {
+              const int idx = (8 * gi + j) * D + f;
+              put_f32(hres, peer_hres, idx, hres[idx] + v[j] + b);
             }
           }
         }
-        cbar_sync();
+        if (!(ok = exchange())) break;
         mark(PF_FF2);
       }
       if (!ok) break;
-      // ---- head.0: Linear + ReLU
-      for (int i = ct; i < CT * D; i += kComputeThreads) {
-        const int n = i / D, f = i - (i / D) * D;
-        tc::store_operand<KIND>(bbuf, n, f, CT, hres[i]);
+      // ---- head.0: Linear + ReLU (own features -> both operands)
+      {
+        uint8_t* buf = bnext();
+        for (int i = ct; i < CT * D; i += kComputeThreads) {
+          const int n = i / D, f = i - (i / D) * D;
+          tc::store_operand<KIND>(buf, n, f, CT, hres[i]);
+        }
       }
       arrive_act();
       mark(PF_HEAD0);
       if (!(ok = wait_mma())) break;
       mark(PF_W_H0);
-      if (g < MT_D) {
-        const int f = g * 128 + row;
-        const float b = f < D ? __ldg(P + o_bh0 + f) : 0.f;
-#pragma unroll 1
-        for (int gi = 0; gi < NG; ++gi) {
+      {
+        uint8_t* buf = bnext();
+        for (int u = g; u < LT_D * NG; u += 4) {
+          const int lt = u / NG, gi = u % NG;
+          const int f = (int)(rank * LT_D + lt) * 128 + row;
           float v[8];
-          tc::tmem_ld8(tq + (uint32_t)(g * CT + 8 * gi), v);
+          tc::tmem_ld8(tq + (uint32_t)(lt * CT + 8 * gi), v);
           if (f < D) {
+            const float b = __ldg(P + o_bh0 + f);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) tc::store_operand<KIND>(bbuf, 8 * gi + j, f, CT, fmaxf(v[j] + b, 0.f));
+            for (int j = 0; j < 8; ++j) put_b(buf, 8 * gi + j, f, fmaxf(v[j] + b, 0.f), true);
           }
         }
       }
@@ -686,27 +818,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       mark(PF_HEAD1);
       if (!(ok = wait_mma())) break;
       mark(PF_W_H2);
-      // ---- head.2: logits -> scratch
-      if (g < 2) {
-        const int vv = g * 128 + row;
+      // ---- head.2: logits (own vocab half) -> both CTAs' scratch
+      for (int u = g; u < LT_V * NG; u += 4) {
+        const int lt = u / NG, gi = u % NG;
+        const int vv = (int)(rank * LT_V + lt) * 128 + row;
         const float b = __ldg(P + o_bh2 + vv);
-#pragma unroll 1
-        for (int gi = 0; gi < NG; ++gi) {
-          float v[8];
-          tc::tmem_ld8(tq + (uint32_t)(g * CT + 8 * gi), v);
+        float v[8];
+        tc::tmem_ld8(tq + (uint32_t)(lt * CT + 8 * gi), v);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) scr[(8 * gi + j) * 256 + vv] = v[j] + b;
-        }
+        for (int j = 0; j < 8; ++j) put_f32(scr, peer_scr, (8 * gi + j) * 256 + vv, v[j] + b);
       }
-      cbar_sync();
+      if (!(ok = exchange())) break;
       mark(PF_HEAD2);
-      // ---- quantiser + range coder, a warp per chunk
+      // ---- quantiser + range coder, a warp per chunk (both CTAs, identical)
       for (int n = cw; n < CT; n += 16) {
         const int c = c0 + n;
         if (!((amask >> n) & 1u)) continue;
         if (mode == MODE_LOGITS) {
-          float* dst = a.logits + ((long long)c * a.n_steps + s) * V;
-          for (int v = lane; v < V; v += 32) dst[v] = scr[n * 256 + v];
+          if (writer) {
+            float* dst = a.logits + ((long long)c * a.n_steps + s) * V;
+            for (int v = lane; v < V; v += 32) dst[v] = scr[n * 256 + v];
+          }
           if (lane == 0) {
             const int nx = (s + 1 < a.n_steps) ? a.tokens[(long long)c * a.n_steps + s + 1] : 0;
             prev[n] = (nx >= 0 && nx < V) ? nx : 0;
@@ -721,15 +853,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         if (mode == MODE_ENCODE) {
           int sym = a.bytes[(long long)c * a.in_pitch + t];
           if (sym >= V) {
-            if (lane == 0) atomicOr(a.err, RC_ERR_SYMBOL);
+            if (lane == 0 && writer) atomicOr(a.err, RC_ERR_SYMBOL);
             sym = 0;
           }
           uint32_t left, freq;
           bq_lookup_warp<8>(fr, base, sym, lane, left, freq);
           if (lane == 0) {
             RcEnc st = encs[n];
-            rc_enc_put(st, left, freq, a.precision, a.words + (long long)c * a.pitch_words, a.pitch_words, a.err);
-            encs[n] = st;
+            if (writer) {
+              rc_enc_put(st, left, freq, a.precision, a.words + (long long)c * a.pitch_words, a.pitch_words, a.err);
+              encs[n] = st;
+            }
             prev[n] = sym;
           }
         } else {
@@ -743,7 +877,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
             nw = nw < 0 ? 0 : (nw > a.pitch_words ? a.pitch_words : nw);
             rc_dec_advance(st, scale, left, freq, a.words_in + (long long)c * a.pitch_words, nw);
             decs[n] = st;
-            a.out[(long long)c * a.out_pitch + t] = (uint8_t)sym;
+            if (writer) a.out[(long long)c * a.out_pitch + t] = (uint8_t)sym;
             prev[n] = sym;
           }
         }
@@ -754,7 +888,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
 #ifdef BOA_PHASE_PROFILE
     if (pon) for (int i = 0; i < 20; ++i) a.prof[i] = pacc[i];
 #endif
-    if (ok && mode == MODE_ENCODE && ct < CT) {
+    if (ok && mode == MODE_ENCODE && ct < CT && writer) {
       const int c = c0 + ct;
       if (c < a.n_chunks) {
         RcEnc st = encs[ct];
@@ -779,6 +913,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
     }
   }
   __syncthreads();
+  // neither CTA of a pair may exit while the peer can still write into it
+  if constexpr (SPLIT == 2) cluster_sync_all();
   if (warp == 1) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
@@ -863,12 +999,13 @@ static uint32_t to_tf32_bits(float f) {
 }
 
 // Append the SW128 tile images of W [M_real x K] (row-major fp32; rows >= M_real
-// and columns >= K_real are zero) as n_mt x n_ks tiles, mt outer.
-static void pack_tiles(std::vector<uint8_t>& out, const float* W, int M_real, int K_real, int ldw, int n_mt,
+// and columns >= K_real are zero): M tiles mt0 .. mt0+n_mt-1, each with n_ks
+// K slices, mt outer.
+static void pack_tiles(std::vector<uint8_t>& out, const float* W, int M_real, int K_real, int ldw, int mt0, int n_mt,
                        int n_ks, int kind) {
   const int eb = kind == 0 ? 4 : 2;
   const int per = 128 / eb;
-  for (int mt = 0; mt < n_mt; ++mt) {
+  for (int mt = mt0; mt < mt0 + n_mt; ++mt) {
     for (int ks = 0; ks < n_ks; ++ks) {
       const size_t base = out.size();
       out.resize(base + kTileBytes, 0);
@@ -904,8 +1041,11 @@ using namespace boa;
 struct boa_model {
   int D, L, V, kind, device;
   int n_sms = 148;
-  TilePlan plan;
-  uint8_t* d_tiles = nullptr;
+  TilePlan plan;              // split 1
+  TilePlan plan2;             // split 2 (valid when has_split2)
+  bool has_split2 = false;
+  uint8_t* d_tiles = nullptr;     // split-1 stream
+  uint8_t* d_tiles2 = nullptr;    // split-2 streams, rank 0 then rank 1
   float* d_params = nullptr;
   uint32_t* d_err = nullptr;
   size_t params_floats = 0;
@@ -926,15 +1066,36 @@ struct FlatReader {
   }
 };
 
+struct LayerW {
+  const float *w_in, *w_x, *w_dt, *w_out, *w1, *w2;
+};
+
+// Pack one rank's weight stream of a `split`-way cluster in consumption order.
+static void pack_stream(std::vector<uint8_t>& tiles, const TilePlan& p, int rank, int D, int V, int kind,
+                        const std::vector<LayerW>& lw, const float* wh0, const float* wh2) {
+  const int E = 2 * D, R = cdiv(D, 16), DBC = R + 32, F = 4 * D;
+  for (const LayerW& w : lw) {
+    pack_tiles(tiles, w.w_in, 2 * E, D, D, rank * p.ltE, p.ltE, p.kD, kind);            // x rows
+    pack_tiles(tiles, w.w_in, 2 * E, D, D, p.mtE + rank * p.ltE, p.ltE, p.kD, kind);    // z rows
+    pack_tiles(tiles, w.w_x, DBC, E, E, 0, 1, p.kE, kind);
+    pack_tiles(tiles, w.w_dt, E, R, R, rank * p.ltE, p.ltE, 1, kind);
+    pack_tiles(tiles, w.w_out, D, E, E, rank * p.ltD, p.ltD, p.kE, kind);
+    pack_tiles(tiles, w.w1, F, D, D, rank * p.ltF, p.ltF, p.kD, kind);
+    pack_tiles(tiles, w.w2, D, F, F, rank * p.ltD, p.ltD, p.kF, kind);
+  }
+  pack_tiles(tiles, wh0, D, D, D, rank * p.ltD, p.ltD, p.kD, kind);
+  pack_tiles(tiles, wh2, V, D, D, rank * p.ltV, p.ltV, p.kD, kind);
+}
+
 template <int D>
 int build_model(boa_model* m, const float* flat, size_t n_floats, std::vector<uint8_t>& tiles,
-                std::vector<float>& params) {
+                std::vector<uint8_t>& tiles2, std::vector<float>& params) {
   using LP = LayerParams<D>;
   const int E = 2 * D, R = cdiv(D, 16), DBC = R + 32, F = 4 * D, V = m->V, L = m->L, kind = m->kind;
-  const TilePlan& p = m->plan;
   FlatReader fr{flat, n_floats};
   const float* emb = fr.take((size_t)V * D);
   params.assign((size_t)LP::stride * L + D + 256 + (size_t)V * D, 0.0f);
+  std::vector<LayerW> lw(L);
   for (int l = 0; l < L; ++l) {
     float* lp = params.data() + (size_t)LP::stride * l;
     const float* ln1w = fr.take(D); const float* ln1b = fr.take(D);
@@ -955,12 +1116,7 @@ int build_model(boa_model* m, const float* flat, size_t n_floats, std::vector<ui
       lp[LP::A2 + i] = (float)(-std::exp((double)A_log[i]) * 1.4426950408889634);
     std::memcpy(lp + LP::ln2w, ln2w, D * 4); std::memcpy(lp + LP::ln2b, ln2b, D * 4);
     std::memcpy(lp + LP::b1, b1, F * 4); std::memcpy(lp + LP::b2, b2, D * 4);
-    pack_tiles(tiles, w_in, 2 * E, D, D, 2 * p.mtE, p.kD, kind);
-    pack_tiles(tiles, w_x, DBC, E, E, 1, p.kE, kind);
-    pack_tiles(tiles, w_dt, E, R, R, p.mtE, 1, kind);
-    pack_tiles(tiles, w_out, D, E, E, p.mtD, p.kE, kind);
-    pack_tiles(tiles, w1, F, D, D, p.mtF, p.kD, kind);
-    pack_tiles(tiles, w2, D, F, F, p.mtD, p.kF, kind);
+    lw[l] = LayerW{w_in, w_x, w_dt, w_out, w1, w2};
   }
   const float* wh0 = fr.take((size_t)D * D); const float* bh0 = fr.take(D);
   const float* wh2 = fr.take((size_t)V * D); const float* bh2 = fr.take(V);
@@ -970,33 +1126,66 @@ int build_model(boa_model* m, const float* flat, size_t n_floats, std::vector<ui
   std::memcpy(g, bh0, D * 4);
   std::memcpy(g + D, bh2, V * 4);
   std::memcpy(g + D + 256, emb, (size_t)V * D * 4);
-  pack_tiles(tiles, wh0, D, D, D, p.mtD, p.kD, kind);
-  pack_tiles(tiles, wh2, V, D, D, 2, p.kD, kind);
-  if (tiles.size() != (size_t)p.per_step * kTileBytes)
+  pack_stream(tiles, m->plan, 0, D, V, kind, lw, wh0, wh2);
+  if (tiles.size() != (size_t)m->plan.per_step * kTileBytes)
     return boa_fail(BOA_ERR_ARG, "boa_model_create: internal tile count mismatch");
+  if (m->has_split2) {
+    pack_stream(tiles2, m->plan2, 0, D, V, kind, lw, wh0, wh2);
+    pack_stream(tiles2, m->plan2, 1, D, V, kind, lw, wh0, wh2);
+    if (tiles2.size() != (size_t)2 * m->plan2.per_step * kTileBytes)
+      return boa_fail(BOA_ERR_ARG, "boa_model_create: internal tile count mismatch (split)");
+  }
   return BOA_OK;
 }
 
 size_t conv_state_bytes(const boa_model* m, int n) { return (size_t)n * m->L * (2 * m->D) * 16; }
 size_t ssm_state_bytes(const boa_model* m, int n) { return (size_t)n * m->L * (2 * m->D) * 64; }
 
-template <int D, int KIND, int CT>
+template <int D, int KIND, int CT, int SPLIT>
 int launch_step_ct(StepArgs& a, int n_chunks, cudaStream_t s) {
-  const int smem = Smem<D, KIND, CT>::ALLOC;
-  BOA_CUDA(cudaFuncSetAttribute(k_boa_step<D, KIND, CT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  const int grid = cdiv(n_chunks, CT);
-  k_boa_step<D, KIND, CT><<<grid, kThreads, smem, s>>>(a);
+  const int smem = Smem<D, KIND, CT, SPLIT>::ALLOC;
+  auto kern = k_boa_step<D, KIND, CT, SPLIT>;
+  BOA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int grid = cdiv(n_chunks, CT) * SPLIT;
+  if constexpr (SPLIT == 1) {
+    kern<<<grid, kThreads, smem, s>>>(a);
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = SPLIT;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    BOA_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+  }
   BOA_CUDA(cudaGetLastError());
   return BOA_OK;
 }
 
+// Pick the decomposition: clusters of two CTAs (half the features each) when
+// 16-chunk tiles would leave SMs idle, 32-chunk tiles when there are chunks
+// enough to fill every SM, 16-chunk single CTAs otherwise.
 template <int D, int KIND>
 int launch_step_t(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
-  if constexpr (ChunkTileMax<D, KIND>::value == 32) {
-    // 32 chunks per CTA only when that still fills every SM
-    if (n_chunks >= 32 * m->n_sms) return launch_step_ct<D, KIND, 32>(a, n_chunks, s);
+  if constexpr (D == 256 && KIND != 0) {
+    if (m->has_split2 && 2 * cdiv(n_chunks, 16) <= m->n_sms) {
+      a.tiles_per_step = m->plan2.per_step;
+      a.wtiles = m->d_tiles2;
+      return launch_step_ct<D, KIND, 16, 2>(a, n_chunks, s);
+    }
   }
-  return launch_step_ct<D, KIND, 16>(a, n_chunks, s);
+  a.tiles_per_step = m->plan.per_step;
+  a.wtiles = m->d_tiles;
+  if constexpr (ChunkTileMax<D, KIND>::value == 32) {
+    if (n_chunks >= 32 * m->n_sms) return launch_step_ct<D, KIND, 32, 1>(a, n_chunks, s);
+  }
+  return launch_step_ct<D, KIND, 16, 1>(a, n_chunks, s);
 }
 
 // BOA_PHASE_PROFILE=1: time the phases of CTA 0 and print them (SM cycles) to stderr.
@@ -1009,8 +1198,6 @@ int launch_step(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
 #endif
   a.n_layers = m->L;
   a.vocab = m->V;
-  a.tiles_per_step = m->plan.per_step;
-  a.wtiles = m->d_tiles;
   a.params = m->d_params;
   a.err = m->d_err;
 #define BOA_DISPATCH(DD)                                            \
@@ -1091,20 +1278,26 @@ BOA_API int boa_model_create(boa_model** out, int d_model, int n_layers, int voc
   BOA_CUDA(cudaSetDevice(device));
   boa_model* m = new boa_model();
   m->D = d_model; m->L = n_layers; m->V = vocab; m->kind = weight_format; m->device = device;
-  m->plan = make_plan(d_model, n_layers, weight_format);
+  m->plan = make_plan(d_model, n_layers, weight_format, 1);
+  m->has_split2 = (d_model == 256 && weight_format != BOA_WEIGHTS_TF32);
+  if (m->has_split2) m->plan2 = make_plan(d_model, n_layers, weight_format, 2);
   cudaDeviceGetAttribute(&m->n_sms, cudaDevAttrMultiProcessorCount, device);
-  std::vector<uint8_t> tiles;
+  std::vector<uint8_t> tiles, tiles2;
   std::vector<float> params;
   int rc = BOA_ERR_UNSUPPORTED;
-  if (d_model == 64) rc = build_model<64>(m, host_flat_weights, n_floats, tiles, params);
-  if (d_model == 256) rc = build_model<256>(m, host_flat_weights, n_floats, tiles, params);
-  if (d_model == 512) rc = build_model<512>(m, host_flat_weights, n_floats, tiles, params);
+  if (d_model == 64) rc = build_model<64>(m, host_flat_weights, n_floats, tiles, tiles2, params);
+  if (d_model == 256) rc = build_model<256>(m, host_flat_weights, n_floats, tiles, tiles2, params);
+  if (d_model == 512) rc = build_model<512>(m, host_flat_weights, n_floats, tiles, tiles2, params);
   if (rc != BOA_OK) { delete m; return rc; }
   m->params_floats = params.size();
   cudaError_t e = cudaMalloc(&m->d_tiles, tiles.size());
   if (e == cudaSuccess) e = cudaMalloc(&m->d_params, params.size() * 4);
   if (e == cudaSuccess) e = cudaMalloc(&m->d_err, 4);
   if (e == cudaSuccess) e = cudaMemcpy(m->d_tiles, tiles.data(), tiles.size(), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && m->has_split2) {
+    e = cudaMalloc(&m->d_tiles2, tiles2.size());
+    if (e == cudaSuccess) e = cudaMemcpy(m->d_tiles2, tiles2.data(), tiles2.size(), cudaMemcpyHostToDevice);
+  }
   if (e == cudaSuccess) e = cudaMemcpy(m->d_params, params.data(), params.size() * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(m->d_err, 0, 4);
   if (e != cudaSuccess) {
@@ -1118,7 +1311,7 @@ BOA_API int boa_model_create(boa_model** out, int d_model, int n_layers, int voc
 BOA_API int boa_model_destroy(boa_model* m) {
   if (!m) return BOA_OK;
   cudaSetDevice(m->device);
-  cudaFree(m->d_tiles); cudaFree(m->d_params); cudaFree(m->d_err);
+  cudaFree(m->d_tiles); cudaFree(m->d_tiles2); cudaFree(m->d_params); cudaFree(m->d_err);
   delete m;
   return BOA_OK;
 }
@@ -1220,7 +1413,7 @@ BOA_API int boa_diag_gemm(int weight_format, int M, int K, const float* h_w, con
     return boa_fail(BOA_ERR_ARG, "boa_diag_gemm: M in {128..512} step 128, K multiple of the slice, <= 1024");
   BOA_CUDA(cudaSetDevice(device));
   std::vector<uint8_t> tiles;
-  pack_tiles(tiles, h_w, M, K, K, M / 128, K / per, weight_format);
+  pack_tiles(tiles, h_w, M, K, K, 0, M / 128, K / per, weight_format);
   uint8_t* d_t = nullptr; float *d_x = nullptr, *d_o = nullptr; uint32_t* d_e = nullptr;
   cudaError_t e = cudaMalloc(&d_t, tiles.size());
   if (e == cudaSuccess) e = cudaMalloc(&d_x, (size_t)kCT * K * 4);

@@ -112,3 +112,19 @@ def test_pitch_overflow_is_an_error():
     lens = torch.full((4,), 500, dtype=torch.int32).cuda()
     with pytest.raises(BoaError):
         codec.encode_device(m, x, lens, pitch_words=8)
+
+
+def test_roundtrip_d256_split_and_single():
+    """d_model 256 with 16-bit weights: a small batch runs as 2-CTA clusters,
+    a large one as single CTAs; streams from either decode in the other."""
+    import codec
+    m = _model(256, 2, "fp16")
+    lens = [60 + (i * 7) % 50 for i in range(40)]
+    xs = _chunks(5, lens)
+    comp, first, Ls = codec.compress_GPU(m, xs)                 # 40 chunks -> clusters
+    outs = codec.decompress_GPU(m, comp, Ls, first)
+    assert all(np.array_equal(x.numpy(), o) for x, o in zip(xs, outs))
+    # the same chunks inside a large batch (single-CTA decomposition)
+    pad = _chunks(6, [60] * 2400)
+    comp2, first2, Ls2 = codec.compress_GPU(m, xs + pad)
+    assert all(np.array_equal(a, b) for a, b in zip(comp, comp2[:40]))
