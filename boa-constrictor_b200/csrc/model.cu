@@ -95,6 +95,7 @@ struct StepArgs {
   int fresh;                // 1: first step starts from zero state (no state loads)
   int precision;
   int tiles_per_step;
+  int tiles_per_layer;
   // encode input
   const uint8_t* bytes; long long in_pitch;
   const int32_t* lens;
@@ -675,12 +676,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
             const float4* A2p = reinterpret_cast<const float4*>(lp + LP::A2) + e * 4;
             const float Dp = __ldg(lp + LP::Dp + e);
             const float bdt = __ldg(lp + LP::dtb + e);
-            float4* ss = a.ssm_state + (((long long)c0 * L + l) * E + e) * 4;   // chunk stride L*E*4
-            const long long cstride = (long long)L * E * 4;
+            // SSM state layout [chunk][layer][k = 0..3][channel] of float4: a
+            // warp's access for one k is 512 contiguous bytes
+            float4* ss = a.ssm_state + ((long long)c0 * L + l) * 4 * E + e;   // chunk stride 4*L*E
+            const long long cstride = (long long)L * 4 * E;
             float4 nx[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              nx[k] = ((lmask >> n0) & 1u) ? ss[n0 * cstride + k] : make_float4(0.f, 0.f, 0.f, 0.f);
+              nx[k] = ((lmask >> n0) & 1u) ? ss[n0 * cstride + k * E] : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
             for (int gi = 0; gi < RUN / 4; ++gi) {
               const int nb = n0 + 4 * gi;
@@ -699,7 +702,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
                 if (n + 1 < n0 + RUN) {
 #pragma unroll
                   for (int k = 0; k < 4; ++k)
-                    nx[k] = ((lmask >> (n + 1)) & 1u) ? ss[(n + 1) * cstride + k] : make_float4(0.f, 0.f, 0.f, 0.f);
+                    nx[k] = ((lmask >> (n + 1)) & 1u) ? ss[(n + 1) * cstride + k * E] : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
                 const float dtv = softplus_f(dtr[j] + bdt);
                 const float dx = dtv * xc[j];
@@ -722,7 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
                 if ((amask >> n) & 1u) {
 #pragma unroll
                   for (int k = 0; k < 4; ++k)
-                    ss[n * cstride + k] = make_float4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
+                    ss[n * cstride + k * E] = make_float4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
                 }
                 y = fmaf(Dp, xc[j], y);
                 y *= silu_fast(z[j]);
@@ -1176,11 +1179,13 @@ int launch_step_t(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s)
   if constexpr (D == 256 && KIND != 0) {
     if (m->has_split2 && 2 * cdiv(n_chunks, 16) <= m->n_sms) {
       a.tiles_per_step = m->plan2.per_step;
+      a.tiles_per_layer = m->plan2.per_layer;
       a.wtiles = m->d_tiles2;
       return launch_step_ct<D, KIND, 16, 2>(a, n_chunks, s);
     }
   }
   a.tiles_per_step = m->plan.per_step;
+  a.tiles_per_layer = m->plan.per_layer;
   a.wtiles = m->d_tiles;
   if constexpr (ChunkTileMax<D, KIND>::value == 32) {
     if (n_chunks >= 32 * m->n_sms) return launch_step_ct<D, KIND, 32, 1>(a, n_chunks, s);
