@@ -365,3 +365,102 @@ BOA_API int boa_rc_decode_step(boa_rc_batch* b, const float* d_rows, int32_t* d_
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free whole-stream encode.
+//
+// Some callers cannot allocate device memory when they code: a host that
+// captures its work into a CUDA graph (cudaMalloc is not allowed while a
+// stream is being captured), a plugin host or real-time service that forbids
+// allocation after start-up, or code that must not fragment a memory pool it
+// does not own.  boa_rc_encode_noalloc serves them: the caller passes the
+// inputs and the outputs, and the per-stream coder state (the scratch that
+// boa_rc_create would allocate) lives in the file-scope array below instead.
+//
+// Limits and sharing:
+//   * at most kNoAllocMaxStreams streams per call (2 MiB of state); larger
+//     calls are rejected with BOA_ERR_ARG;
+//   * the array is one per device and every call shares it: each call clears
+//     the state of the streams it uses (and the error word) before coding, so
+//     nothing from an earlier call leaks in, but two calls that overlap on the
+//     GPU (different streams, different host threads) race on it and corrupt
+//     each other's output;
+//   * every GPU that loads this library keeps the array until process exit;
+//   * the first call on a device looks up the array's device address
+//     (cudaGetSymbolAddress); make that first call before any stream capture.
+// ---------------------------------------------------------------------------
+namespace boa {
+constexpr int kNoAllocMaxStreams = 1 << 16;
+constexpr size_t kNoAllocStateBytes = (size_t)kNoAllocMaxStreams * sizeof(RcEnc);
+static __device__ __align__(256) unsigned char g_rc_noalloc_scratch[kNoAllocStateBytes + 256];
+}  // namespace boa
+
+#include <mutex>
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64] = {nullptr};
+
+// Device address of the scratch array on the current device (looked up once).
+static int noalloc_scratch(int device, void** out) {
+  if (device < 0 || device >= 64) return boa_fail(BOA_ERR_ARG, "boa_rc_encode_noalloc: device index out of range");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, boa::g_rc_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return boa_fail(BOA_ERR_CUDA, std::string("boa_rc_encode_noalloc: cudaGetSymbolAddress: ") +
+                                        cudaGetErrorString(e));
+    g_noalloc_ptr[device] = p;
+  }
+  *out = g_noalloc_ptr[device];
+  return BOA_OK;
+}
+
+__global__ void k_rc_noalloc_clear(RcEnc* enc, int n, uint32_t* err) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) rc_enc_reset(enc[i]);
+  if (i == 0) *err = 0u;
+}
+
+extern "C" BOA_API int boa_rc_encode_noalloc(int n_streams, int k_symbols, int n_steps, int precision,
+                                             const float* d_logits, const int32_t* d_symbols, const uint8_t* d_mask,
+                                             uint32_t* d_words, int pitch_words, int32_t* d_sizes, void* stream) {
+  if (n_streams < 1 || n_streams > kNoAllocMaxStreams)
+    return boa_fail(BOA_ERR_ARG, "boa_rc_encode_noalloc: n_streams must be in [1, 65536] (static scratch limit)");
+  if (k_symbols < 1 || k_symbols > 1024) return boa_fail(BOA_ERR_ARG, "boa_rc_encode_noalloc: K must be in [1, 1024]");
+  if (n_steps < 0 || pitch_words < 1) return boa_fail(BOA_ERR_ARG, "boa_rc_encode_noalloc: bad n_steps / pitch");
+  if (precision < 11 || precision > 24 || 2 * k_symbols > (1 << precision))
+    return boa_fail(BOA_ERR_ARG, "boa_rc_encode_noalloc: precision out of range for K");
+  if (!d_words || !d_sizes || (n_steps > 0 && (!d_logits || !d_symbols)))
+    return boa_fail(BOA_ERR_ARG, "boa_rc_encode_noalloc: null argument");
+  int device = 0;
+  BOA_CUDA(cudaGetDevice(&device));
+  void* base = nullptr;
+  int rc = noalloc_scratch(device, &base);
+  if (rc) return rc;
+  RcEnc* enc = reinterpret_cast<RcEnc*>(base);
+  uint32_t* err = reinterpret_cast<uint32_t*>(reinterpret_cast<unsigned char*>(base) + kNoAllocStateBytes);
+  cudaStream_t s = (cudaStream_t)stream;
+  k_rc_noalloc_clear<<<(n_streams + 255) / 256, 256, 0, s>>>(enc, n_streams, err);
+  BOA_CUDA(cudaGetLastError());
+  const int grid = rc_grid_warps(n_streams);
+  for (int t = 0; t < n_steps; ++t) {
+    const float* rows = d_logits + (size_t)t * n_streams * k_symbols;
+    const int32_t* syms = d_symbols + (size_t)t * n_streams;
+    const uint8_t* mask = d_mask ? d_mask + (size_t)t * n_streams : nullptr;
+    if (k_symbols <= 256)
+      k_rc_encode_bq<8><<<grid, 256, 0, s>>>(n_streams, k_symbols, precision, rows, syms, mask, enc, d_words,
+                                             pitch_words, err);
+    else
+      k_rc_encode_bq<32><<<grid, 256, 0, s>>>(n_streams, k_symbols, precision, rows, syms, mask, enc, d_words,
+                                              pitch_words, err);
+  }
+  k_rc_finalize<<<(n_streams + 127) / 128, 128, 0, s>>>(n_streams, enc, d_words, pitch_words, d_sizes, err);
+  BOA_CUDA(cudaGetLastError());
+  uint32_t e = 0;
+  BOA_CUDA(cudaMemcpyAsync(&e, err, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+  BOA_CUDA(cudaStreamSynchronize(s));
+  if (e & RC_ERR_OVERFLOW) return boa_fail(BOA_ERR_OVERFLOW, "boa_rc_encode_noalloc: a stream exceeded its pitch");
+  if (e & RC_ERR_SYMBOL) return boa_fail(BOA_ERR_ARG, "boa_rc_encode_noalloc: symbol outside [0, K)");
+  return BOA_OK;
+}

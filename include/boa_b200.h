@@ -94,6 +94,22 @@ BOA_API int boa_rc_init_decoder(boa_rc_batch* b, void* stream);
 BOA_API int boa_rc_decode_step(boa_rc_batch* b, const float* d_rows, int32_t* d_out_symbols,
                                const uint8_t* d_mask, void* stream);
 
+/* Allocation-free whole-stream encode (no counterpart in the reference).
+ * For callers that cannot allocate device memory while they code (work being
+ * captured into a CUDA graph, hosts that forbid allocation after start-up):
+ * codes n_steps symbols of each of n_streams streams with the BQ quantiser,
+ * then finalises, using a static per-device scratch array (2 MiB) for the
+ * coder state instead of memory from boa_rc_create.  d_logits is
+ * [n_steps][n_streams][K] fp32, d_symbols [n_steps][n_streams] int32, d_mask
+ * [n_steps][n_streams] u8 or NULL; writes d_words [n_streams][pitch_words] and
+ * d_sizes[n_streams].  At most 65536 streams (BOA_ERR_ARG beyond).  Calls
+ * share the scratch: calls that overlap on the GPU race.  The first call on a
+ * device looks up the scratch address; make it before any stream capture.
+ * Synchronises `stream` to report overflow. */
+BOA_API int boa_rc_encode_noalloc(int n_streams, int k_symbols, int n_steps, int precision,
+                                  const float* d_logits, const int32_t* d_symbols, const uint8_t* d_mask,
+                                  uint32_t* d_words, int pitch_words, int32_t* d_sizes, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* BoaConstrictor model (model.py:5-134).                                   */
 /* ------------------------------------------------------------------------ */
