@@ -1024,11 +1024,11 @@ static void pack_tiles(std::vector<uint8_t>& out, const float* W, int M_real, in
           if (kind == 0) {
             const uint32_t b = to_tf32_bits(v);
             std::memcpy(p, &b, 4);
-          } else if (kind == 1) {
-            const unsigned short h = __half_as_ushort(__float2half_rn(v));
+          } else if (kind == BOA_WEIGHTS_BF16) {
+            const unsigned short h = __bfloat16_as_ushort(__float2bfloat16_rn(v));
             std::memcpy(p, &h, 2);
           } else {
-            const unsigned short h = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+            const unsigned short h = __half_as_ushort(__float2half_rn(v));
             std::memcpy(p, &h, 2);
           }
         }

@@ -182,7 +182,7 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
   return d;
 }
 
-// Operand kinds: 0 = tf32 (fp32 storage), 1 = fp16, 2 = bf16.
+// Operand kinds (the BOA_WEIGHTS_* values): 0 = tf32 (fp32 storage), 1 = bf16, 2 = fp16.
 template <int KIND>
 struct OpKind;
 template <>
@@ -193,12 +193,12 @@ struct OpKind<0> {
 template <>
 struct OpKind<1> {
   static constexpr int kElemBytes = 2;
-  static constexpr uint32_t kFmt = 0;  // F16
+  static constexpr uint32_t kFmt = 1;  // BF16
 };
 template <>
 struct OpKind<2> {
   static constexpr int kElemBytes = 2;
-  static constexpr uint32_t kFmt = 1;  // BF16
+  static constexpr uint32_t kFmt = 0;  // F16
 };
 
 // Instruction descriptor: D fp32, A/B K-major, no negation/sparsity.
@@ -253,9 +253,9 @@ __device__ __forceinline__ void store_operand(uint8_t* buf, int row, int k, int 
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(v));
     *reinterpret_cast<uint32_t*>(p) = t;
   } else if constexpr (KIND == 1) {
-    *reinterpret_cast<unsigned short*>(p) = __half_as_ushort(__float2half_rn(v));
-  } else {
     *reinterpret_cast<unsigned short*>(p) = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  } else {
+    *reinterpret_cast<unsigned short*>(p) = __half_as_ushort(__float2half_rn(v));
   }
 }
 

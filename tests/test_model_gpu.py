@@ -12,7 +12,7 @@ from oracle import model_oracle as mo
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("fmt,tol", [(0, 2e-3), (1, 2e-3), (2, 1.6e-2)])
+@pytest.mark.parametrize("fmt,tol", [(0, 2e-3), (1, 1.6e-2), (2, 2e-3)])   # tf32, bf16, fp16
 @pytest.mark.parametrize("M,K", [(128, 64), (256, 256), (512, 1024)])
 def test_diag_gemm(fmt, tol, M, K):
     rng = np.random.default_rng(M + K + fmt)
