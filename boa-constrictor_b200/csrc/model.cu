@@ -49,6 +49,7 @@ namespace boa {
 
 constexpr int kTileBytes = 16384;      // one A tile: 128 rows x 128 bytes
 constexpr int kComputeThreads = 512;   // warps 2..17
+constexpr int kComputeWarps = kComputeThreads / 32;
 constexpr int kThreads = 576;
 constexpr int kCT = 16;                // chunks per CTA of the diagnostic GEMM
 constexpr long long kWaitBudget = 4000000000LL;  // SM clock cycles per bounded wait (~2 s)
@@ -244,11 +245,22 @@ __device__ __forceinline__ void fence_proxy_async_cluster() {
 // the weights, and writes every value the peer needs into the peer's shared
 // memory as well (DSMEM).  LayerNorms and the coder run redundantly in both
 // CTAs on identical data; CTA 0 writes the codec outputs.
-template <int D, int KIND, int CT_, int SPLIT>
+// TB > 1 is the time-blocked form of encode and logits mode: the CT operand
+// columns are CT / TB chunks x TB consecutive positions (column n = chunk
+// n / TB, position offset n % TB), so one pass of the weights serves TB
+// positions and each chunk's recurrent state is read and written once per TB
+// positions.  The conv window and the SSM state carry from one position to
+// the next in registers, and every column goes through the same arithmetic
+// as in the one-position step, so the logits, and hence the bitstream, are
+// bit for bit those of the TB = 1 kernel that decode uses.
+template <int D, int KIND, int CT_, int SPLIT, int TB>
 __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant__ StepArgs a) {
   using S = Smem<D, KIND, CT_, SPLIT>;
   using LP = LayerParams<D>;
   constexpr int CT = S::CT;
+  constexpr int CHUNKS = CT / TB;                        // chunks per CTA (per cluster when SPLIT == 2)
+  static_assert(TB == 1 || TB == 2 || TB == 4 || TB == 8, "time block");
+  static_assert(TB == 1 || SPLIT == 1, "time blocks run on single CTAs");
   constexpr int NG = CT / 8;                             // groups of 8 chunks
   constexpr int kStagesK = S::STAGES;
   constexpr int E = 2 * D, R = (D + 15) / 16, DBC = R + 32, F = 4 * D;
@@ -267,6 +279,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   constexpr int RUNS = LT_E >= 4 ? 1 : 4 / LT_E;         // chunk runs per local channel tile
   constexpr int RUN = CT / RUNS;
   static_assert(RUN % 4 == 0 && RUN >= 4, "chunk run");
+  static_assert(RUN % TB == 0, "a chunk run holds whole time blocks");
+  // column masks: first / last position of each chunk's time block
+  constexpr uint32_t kColAll = CT == 32 ? 0xffffffffu : ((1u << CT) - 1u);
+  constexpr uint32_t kFirstCols = [] {
+    uint32_t m = 0;
+    for (int n = 0; n < CT; n += TB) m |= 1u << n;
+    return m;
+  }();
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -294,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   const int lane = tid & 31;
   const uint32_t rank = SPLIT == 2 ? cluster_rank() : 0u;
   const uint32_t peer = rank ^ 1u;
-  const int c0 = (blockIdx.x / SPLIT) * CT;
+  const int c0 = (blockIdx.x / SPLIT) * CHUNKS;         // first chunk; column n codes chunk c0 + n / TB
   const int mode = a.mode;
   const int L = a.n_layers;
   const int V = a.vocab;
@@ -308,9 +328,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   if (tid == 0) {
     for (int s = 0; s < kStagesK; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
     tc::mbar_init(mma_bar, 1);
-    tc::mbar_init(act_bar, kComputeThreads * SPLIT);      // both CTAs' compute threads
+    tc::mbar_init(act_bar, kComputeWarps * SPLIT);        // both CTAs' compute warps (lane 0 of each)
     tc::mbar_init(drain_bar, 1);
-    tc::mbar_init(xch_bar, kComputeThreads);              // the peer's compute threads
+    tc::mbar_init(xch_bar, kComputeWarps);                // the peer's compute warps
     *abort_flag = 0;
     *cons_sh = 0;
     *prod_it_sh = 0;
@@ -318,12 +338,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
     if (mode == MODE_LOGITS) {
       ns = a.n_steps;
     } else {
-      for (int n = 0; n < CT; ++n) {
+      for (int n = 0; n < CHUNKS; ++n) {
         const int c = c0 + n;
         if (c < a.n_chunks) ns = max(ns, a.lens[c] - 1);
       }
     }
-    *nsteps_sh = ns;
+    *nsteps_sh = (ns + TB - 1) / TB;                      // steps of TB positions
     tc::fence_barrier_init();
   }
   if (warp == 1) {
@@ -332,13 +352,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   }
   if (tid >= 64 && tid < 64 + CT) {
     const int n = tid - 64;
-    const int c = c0 + n;
+    const int c = c0 + n / TB, jj = n % TB;
     int p0 = 0, len = 0;
     if (c < a.n_chunks) {
       if (mode == MODE_ENCODE) {
         len = a.lens[c];
-        p0 = a.bytes[(long long)c * a.in_pitch];
-        rc_enc_reset(reinterpret_cast<RcEnc*>(smem + S::o_enc)[n]);
+        p0 = jj < len ? a.bytes[(long long)c * a.in_pitch + jj] : 0;
+        if (jj == 0) rc_enc_reset(reinterpret_cast<RcEnc*>(smem + S::o_enc)[n / TB]);
       } else if (mode == MODE_DECODE) {
         len = a.lens[c];
         p0 = a.first_bytes[c];
@@ -347,8 +367,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         rc_dec_reset(reinterpret_cast<RcDec*>(smem + S::o_enc)[n], a.words_in + (long long)c * a.pitch_words, nw);
         if (writer) a.out[(long long)c * a.out_pitch] = (uint8_t)p0;
       } else {
-        len = 0x7fffffff;
-        p0 = a.tokens[(long long)c * a.n_steps];
+        len = a.n_steps;
+        p0 = jj < a.n_steps ? a.tokens[(long long)c * a.n_steps + jj] : 0;
       }
     }
     prev[n] = (p0 >= 0 && p0 < V) ? p0 : 0;
@@ -523,12 +543,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       arr[idx] = v;
       if constexpr (SPLIT == 2) st_cluster_b32(peer_arr + 4u * (uint32_t)idx, __float_as_uint(v));
     };
+    // Every thread orders its operand writes (and TMEM reads) before the
+    // warp barrier; lane 0 then arrives once for the warp, which keeps the
+    // barrier traffic at 16 arrivals per CTA instead of 512.
     auto arrive_act = [&]() {
       if constexpr (SPLIT == 2) fence_proxy_async_cluster();
       else tc::fence_proxy_async_smem();
       tc::tc_fence_before();
-      tc::mbar_arrive(act_bar);
-      if constexpr (SPLIT == 2) mbar_arrive_remote(peer_act);
+      __syncwarp();
+      if (lane == 0) {
+        tc::mbar_arrive(act_bar);
+        if constexpr (SPLIT == 2) mbar_arrive_remote(peer_act);
+      }
       ++gemm_no;
     };
     // Wait for the GEMM just issued; the verdict is uniform over the 512 threads.
@@ -543,7 +569,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
     // values to have arrived here.  Uniform verdict as wait_mma.
     auto exchange = [&]() -> bool {
       if constexpr (SPLIT == 2) {
-        mbar_arrive_remote(peer_xch);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(peer_xch);
         mbar_wait_cluster(xch_bar, xch_phase, abort_flag, kWaitBudget);
         xch_phase ^= 1u;
       }
@@ -579,13 +606,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
 
     bool ok = true;
     for (int s = 0; s < nsteps && ok; ++s) {
-      const int t = (mode == MODE_LOGITS) ? s : s + 1;     // position predicted / coded
+      // column n predicts / codes position t0 + n % TB
+      const int t0 = (mode == MODE_LOGITS) ? s * TB : s * TB + 1;
       const bool load_state = !(a.fresh && s == 0);
-      // active mask of this step (bit n: chunk n codes position t)
+      // active mask of this step (bit n: column n codes a position of its chunk)
       uint32_t amask = 0;
 #pragma unroll
-      for (int n = 0; n < CT; ++n) amask |= (t < lens_sh[n] ? 1u : 0u) << n;
-      const uint32_t lmask = load_state ? amask : 0u;
+      for (int n = 0; n < CT; ++n) amask |= (t0 + n % TB < lens_sh[n] ? 1u : 0u) << n;
+      // state is read at a chunk's first column and written after its last
+      // one, for chunks that are still running in this step
+      const uint32_t lmask = load_state ? (amask & kFirstCols) : 0u;
+      const uint32_t smask = ((amask & kFirstCols) << (TB - 1)) & kColAll;
       // ---- embedding (both CTAs, whole rows)
       for (int i = ct; i < CT * D; i += kComputeThreads) {
         const int n = i / D, f = i - (i / D) * D;
@@ -613,24 +644,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
             float4* cs = a.conv_state + ((long long)c0 * L + l) * E + e;   // chunk stride L*E
             const long long cst = (long long)L * E;
             {
-              const int nb = (u % NG) * 8;
-              float4 stv[8];
+              const int nb = (u % NG) * 8;                  // 8 columns = 8 / TB whole chunks
+              float4 stv[8 / TB];
 #pragma unroll
-              for (int j = 0; j < 8; ++j)
-                stv[j] = ((lmask >> (nb + j)) & 1u) ? cs[(nb + j) * cst] : make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int j = 0; j < 8; j += TB)
+                stv[j / TB] = ((lmask >> (nb + j)) & 1u) ? cs[((nb + j) / TB) * cst] : make_float4(0.f, 0.f, 0.f, 0.f);
               float xv[8];
               const uint32_t col = (uint32_t)(COL_X + lt * CT + nb);
               tc::tmem_ld8(tq + col, xv);
+              float4 win = stv[0];                          // window (x[t-3], x[t-2], x[t-1]) of column nb
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
                 const int n = nb + j;
+                if (j % TB == 0) win = stv[j / TB];
                 float acc = cb;
-                acc = fmaf(w.x, stv[j].x, acc);
-                acc = fmaf(w.y, stv[j].y, acc);
-                acc = fmaf(w.z, stv[j].z, acc);
+                acc = fmaf(w.x, win.x, acc);
+                acc = fmaf(w.y, win.y, acc);
+                acc = fmaf(w.z, win.z, acc);
                 acc = fmaf(w.w, xv[j], acc);
                 const float xc = silu_fast(acc);
-                if ((amask >> n) & 1u) cs[n * cst] = make_float4(stv[j].y, stv[j].z, xv[j], 0.f);
+                win = make_float4(win.y, win.z, xv[j], 0.f);
+                if ((smask >> n) & 1u) cs[(n / TB) * cst] = win;
                 put_b(buf, n, e, xc, true);
                 xv[j] = xc;
               }
@@ -680,10 +714,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
             // warp's access for one k is 512 contiguous bytes
             float4* ss = a.ssm_state + ((long long)c0 * L + l) * 4 * E + e;   // chunk stride 4*L*E
             const long long cstride = (long long)L * 4 * E;
-            float4 nx[4];
+            float4 nx[4];                                   // state of the next chunk, loaded one chunk ahead
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              nx[k] = ((lmask >> n0) & 1u) ? ss[n0 * cstride + k * E] : make_float4(0.f, 0.f, 0.f, 0.f);
+              nx[k] = ((lmask >> n0) & 1u) ? ss[(n0 / TB) * cstride + k * E] : make_float4(0.f, 0.f, 0.f, 0.f);
+            float h[16];
 #pragma unroll 1
             for (int gi = 0; gi < RUN / 4; ++gi) {
               const int nb = n0 + 4 * gi;
@@ -694,15 +729,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const int n = nb + j;
-                float h[16];
+                if (n % TB == 0) {                          // first position of a chunk: take its state
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  h[4 * k] = nx[k].x; h[4 * k + 1] = nx[k].y; h[4 * k + 2] = nx[k].z; h[4 * k + 3] = nx[k].w;
-                }
-                if (n + 1 < n0 + RUN) {
+                  for (int k = 0; k < 4; ++k) {
+                    h[4 * k] = nx[k].x; h[4 * k + 1] = nx[k].y; h[4 * k + 2] = nx[k].z; h[4 * k + 3] = nx[k].w;
+                  }
+                  if (n + TB < n0 + RUN) {
 #pragma unroll
-                  for (int k = 0; k < 4; ++k)
-                    nx[k] = ((lmask >> (n + 1)) & 1u) ? ss[(n + 1) * cstride + k * E] : make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int k = 0; k < 4; ++k)
+                      nx[k] = ((lmask >> (n + TB)) & 1u) ? ss[((n + TB) / TB) * cstride + k * E]
+                                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+                  }
                 }
                 const float dtv = softplus_f(dtr[j] + bdt);
                 const float dx = dtv * xc[j];
@@ -722,10 +759,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
                   y = fmaf(h[4 * k + 2], C4.z, y);
                   y = fmaf(h[4 * k + 3], C4.w, y);
                 }
-                if ((amask >> n) & 1u) {
+                if ((smask >> n) & 1u) {
 #pragma unroll
                   for (int k = 0; k < 4; ++k)
-                    ss[n * cstride + k * E] = make_float4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
+                    ss[(n / TB) * cstride + k * E] = make_float4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
                 }
                 y = fmaf(Dp, xc[j], y);
                 y *= silu_fast(z[j]);
@@ -833,17 +870,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       }
       if (!(ok = exchange())) break;
       mark(PF_HEAD2);
-      // ---- quantiser + range coder, a warp per chunk (both CTAs, identical)
-      for (int n = cw; n < CT; n += 16) {
-        const int c = c0 + n;
+      // ---- quantiser + range coder, a warp per chunk (both CTAs, identical);
+      //      a chunk's TB positions are coded in order
+      for (int ch = cw; ch < CHUNKS; ch += 16)
+#pragma unroll 1
+      for (int jj = 0; jj < TB; ++jj) {
+        const int n = ch * TB + jj;
+        const int c = c0 + ch;
+        const int t = t0 + jj;                             // position predicted / coded by column n
         if (!((amask >> n) & 1u)) continue;
         if (mode == MODE_LOGITS) {
           if (writer) {
-            float* dst = a.logits + ((long long)c * a.n_steps + s) * V;
+            float* dst = a.logits + ((long long)c * a.n_steps + t) * V;
             for (int v = lane; v < V; v += 32) dst[v] = scr[n * 256 + v];
           }
           if (lane == 0) {
-            const int nx = (s + 1 < a.n_steps) ? a.tokens[(long long)c * a.n_steps + s + 1] : 0;
+            const int nt = t + TB;                         // this column's position in the next step
+            const int nx = (nt < a.n_steps) ? a.tokens[(long long)c * a.n_steps + nt] : 0;
             prev[n] = (nx >= 0 && nx < V) ? nx : 0;
           }
           continue;
@@ -862,14 +905,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
           uint32_t left, freq;
           bq_lookup_warp<8>(fr, base, sym, lane, left, freq);
           if (lane == 0) {
-            RcEnc st = encs[n];
+            RcEnc st = encs[n / TB];
             if (writer) {
               rc_enc_put(st, left, freq, a.precision, a.words + (long long)c * a.pitch_words, a.pitch_words, a.err);
-              encs[n] = st;
+              encs[n / TB] = st;
             }
-            prev[n] = sym;
+            if constexpr (TB == 1) {
+              prev[n] = sym;
+            } else {                                       // input of this column in the next step
+              const int nt = t + TB - 1;
+              const int nx = nt < lens_sh[n] ? a.bytes[(long long)c * a.in_pitch + nt] : 0;
+              prev[n] = nx < V ? nx : 0;
+            }
           }
-        } else {
+        } else if constexpr (TB == 1) {
           RcDec st = decs[n];
           unsigned long long scale;
           const uint32_t target = rc_dec_target(st, a.precision, scale);
@@ -891,7 +940,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
 #ifdef BOA_PHASE_PROFILE
     if (pon) for (int i = 0; i < 20; ++i) a.prof[i] = pacc[i];
 #endif
-    if (ok && mode == MODE_ENCODE && ct < CT && writer) {
+    if (ok && mode == MODE_ENCODE && ct < CHUNKS && writer) {
       const int c = c0 + ct;
       if (c < a.n_chunks) {
         RcEnc st = encs[ct];
@@ -1052,6 +1101,7 @@ struct boa_model {
   float* d_params = nullptr;
   uint32_t* d_err = nullptr;
   size_t params_floats = 0;
+  int time_block = 4;             // positions per step in encode / logits mode (1 or 4)
 };
 
 namespace {
@@ -1144,12 +1194,12 @@ int build_model(boa_model* m, const float* flat, size_t n_floats, std::vector<ui
 size_t conv_state_bytes(const boa_model* m, int n) { return (size_t)n * m->L * (2 * m->D) * 16; }
 size_t ssm_state_bytes(const boa_model* m, int n) { return (size_t)n * m->L * (2 * m->D) * 64; }
 
-template <int D, int KIND, int CT, int SPLIT>
+template <int D, int KIND, int CT, int SPLIT, int TB = 1>
 int launch_step_ct(StepArgs& a, int n_chunks, cudaStream_t s) {
   const int smem = Smem<D, KIND, CT, SPLIT>::ALLOC;
-  auto kern = k_boa_step<D, KIND, CT, SPLIT>;
+  auto kern = k_boa_step<D, KIND, CT, SPLIT, TB>;
   BOA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  const int grid = cdiv(n_chunks, CT) * SPLIT;
+  const int grid = cdiv(n_chunks, CT / TB) * SPLIT;
   if constexpr (SPLIT == 1) {
     kern<<<grid, kThreads, smem, s>>>(a);
   } else {
@@ -1171,11 +1221,22 @@ int launch_step_ct(StepArgs& a, int n_chunks, cudaStream_t s) {
   return BOA_OK;
 }
 
-// Pick the decomposition: clusters of two CTAs (half the features each) when
-// 16-chunk tiles would leave SMs idle, 32-chunk tiles when there are chunks
-// enough to fill every SM, 16-chunk single CTAs otherwise.
+// Pick the decomposition.  Encode and logits runs of at least 4 positions use
+// time blocks of 4 positions on the widest single-CTA tile (32 columns = 8
+// chunks with 16-bit operands at d_model <= 256, else 16 columns = 4 chunks).
+// Decode, and single steps, use one position per step: clusters of two CTAs
+// (half the features each) when 16-chunk tiles would leave SMs idle, 32-chunk
+// tiles when there are chunks enough to fill every SM, 16-chunk single CTAs
+// otherwise.  Every choice gives the same per-column arithmetic.
 template <int D, int KIND>
-int launch_step_t(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
+int launch_step_t(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s, int positions) {
+  if (m->time_block == 4 && positions >= 4 && (a.mode == MODE_ENCODE || a.mode == MODE_LOGITS)) {
+    a.tiles_per_step = m->plan.per_step;
+    a.tiles_per_layer = m->plan.per_layer;
+    a.wtiles = m->d_tiles;
+    if constexpr (ChunkTileMax<D, KIND>::value == 32) return launch_step_ct<D, KIND, 32, 1, 4>(a, n_chunks, s);
+    else return launch_step_ct<D, KIND, 16, 1, 4>(a, n_chunks, s);
+  }
   if constexpr (D == 256 && KIND != 0) {
     if (m->has_split2 && 2 * cdiv(n_chunks, 16) <= m->n_sms) {
       a.tiles_per_step = m->plan2.per_step;
@@ -1205,11 +1266,12 @@ int launch_step(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
   a.vocab = m->V;
   a.params = m->d_params;
   a.err = m->d_err;
+  const int positions = a.mode == MODE_LOGITS ? a.n_steps : 0x7fffffff;
 #define BOA_DISPATCH(DD)                                            \
   if (m->D == DD) {                                                 \
-    if (m->kind == 0) return launch_step_t<DD, 0>(m, a, n_chunks, s); \
-    if (m->kind == 1) return launch_step_t<DD, 1>(m, a, n_chunks, s); \
-    return launch_step_t<DD, 2>(m, a, n_chunks, s);                 \
+    if (m->kind == 0) return launch_step_t<DD, 0>(m, a, n_chunks, s, positions); \
+    if (m->kind == 1) return launch_step_t<DD, 1>(m, a, n_chunks, s, positions); \
+    return launch_step_t<DD, 2>(m, a, n_chunks, s, positions);                 \
   }
   BOA_DISPATCH(64)
   BOA_DISPATCH(256)
@@ -1326,6 +1388,13 @@ BOA_API size_t boa_model_workspace_bytes(const boa_model* m, int n_chunks) {
   // state is addressed per CTA tile of up to 32 chunks, so round the count up
   const int n = cdiv(n_chunks, 32) * 32;
   return conv_state_bytes(m, n) + ssm_state_bytes(m, n);
+}
+
+BOA_API int boa_model_set_time_block(boa_model* m, int positions) {
+  if (!m || (positions != 1 && positions != 4))
+    return boa_fail(BOA_ERR_ARG, "boa_model_set_time_block: positions must be 1 or 4");
+  m->time_block = positions;
+  return BOA_OK;
 }
 
 BOA_API int boa_model_info(const boa_model* m, int* d_model, int* n_layers, int* vocab, int* weight_format,

@@ -98,6 +98,10 @@ class NativeModel:
     def workspace_bytes(self, n: int) -> int:
         return int(_n.load().boa_model_workspace_bytes(self.h, int(n)))
 
+    def set_time_block(self, positions: int) -> None:
+        """Positions per kernel step for encode / logits runs: 4 (default) or 1."""
+        _n.call("boa_model_set_time_block", self.h, int(positions))
+
     def tile_bytes_per_step(self) -> int:
         v = ctypes.c_size_t()
         _n.call("boa_model_info", self.h, None, None, None, None, ctypes.byref(v))

@@ -129,6 +129,12 @@ BOA_API int boa_model_info(const boa_model* m, int* d_model, int* n_layers, int*
 /* Bytes of device workspace (recurrent state + bookkeeping) that one
  * boa_codec_* / boa_model_logits call over n_chunks streams needs. */
 BOA_API size_t boa_model_workspace_bytes(const boa_model* m, int n_chunks);
+/* Positions per kernel step for encode and for logits runs of 4 or more
+ * positions: 4 (default; the weights and each chunk's recurrent state are read
+ * once per 4 positions) or 1 (one position per step, as decode).  Outputs are
+ * bit for bit the same either way.  No reference counterpart: the reference
+ * codec (codec.py:56-79) always steps one position at a time. */
+BOA_API int boa_model_set_time_block(boa_model* m, int positions);
 
 /* Reference-shaped single step: the streaming state of init_stream/step
  * (model.py:104-117) lives in d_workspace (zero it to start a stream).

@@ -128,3 +128,24 @@ def test_roundtrip_d256_split_and_single():
     pad = _chunks(6, [60] * 2400)
     comp2, first2, Ls2 = codec.compress_GPU(m, xs + pad)
     assert all(np.array_equal(a, b) for a, b in zip(comp, comp2[:40]))
+
+
+@pytest.mark.parametrize("d,fmt", [(64, "tf32"), (256, "fp16")])
+def test_time_blocked_encode_matches_one_position_steps(d, fmt):
+    """Encode in time blocks of 4 positions (the default) writes the same
+    words as encode one position per kernel step, for lengths that end at
+    every offset inside a block; decode (always one position per step) reads
+    them back."""
+    import codec
+    m = _model(d, 2, fmt)
+    nm = m.native(torch.device("cuda", 0))
+    lens = [1, 2, 3, 4, 5, 6, 7, 8, 9, 63, 64, 65, 130] * 3
+    xs = _chunks(9, lens)
+    nm.set_time_block(1)
+    comp1, first1, Ls1 = codec.compress_GPU(m, xs)
+    nm.set_time_block(4)
+    comp4, first4, Ls4 = codec.compress_GPU(m, xs)
+    assert first1 == first4 and Ls1 == Ls4
+    assert all(np.array_equal(a, b) for a, b in zip(comp1, comp4))
+    outs = codec.decompress_GPU(m, comp4, Ls4, first4)
+    assert all(np.array_equal(x.numpy(), o) for x, o in zip(xs, outs))

@@ -79,17 +79,25 @@ def test_step_matches_forward():
 @pytest.mark.parametrize("fmt", ["fp16", "bf16"])
 def test_logits_identical_across_decompositions(fmt):
     """The host picks a kernel decomposition from the batch size (2-CTA
-    clusters with 16 chunks, single CTAs with 16 chunks, or 32-chunk tiles);
-    every one must give the same bits for the same chunk, or a file coded in
-    one batch shape would not decode in another."""
+    clusters with 16 chunks, single CTAs with 16 chunks, or 32-chunk tiles)
+    and, for encode and logits runs, time blocks of 4 positions; every one
+    must give the same bits for the same chunk, or a file coded in one batch
+    shape would not decode in another."""
     from model import seeded_model
     m = seeded_model(256, 2, weight_format=fmt)
+    nm = m.native(torch.device("cuda", 0))
     rng = np.random.default_rng(11)
     base = rng.integers(0, 256, (20, 6)).astype(np.int64)
+    nm.set_time_block(1)                                             # one position per kernel step
     small = _native_logits(m, base)                                  # 2 x ceil(20/16) CTAs: split clusters
     mid = np.concatenate([base, rng.integers(0, 256, (2400 - 20, 6))])
     big = np.concatenate([base, rng.integers(0, 256, (4800 - 20, 6))])
     got_mid = _native_logits(m, mid)[:20]                            # 150 tiles of 16: single CTAs
     got_big = _native_logits(m, big)[:20]                            # >= 32 x SMs chunks: 32-chunk tiles
+    nm.set_time_block(4)                                             # 8 chunks x 4 positions per CTA
+    got_tb = _native_logits(m, base)                                 # 6 positions: one full, one partial block
+    got_tb_mid = _native_logits(m, mid)[:20]
     assert torch.equal(small, got_mid)
     assert torch.equal(small, got_big)
+    assert torch.equal(small, got_tb)
+    assert torch.equal(small, got_tb_mid)
