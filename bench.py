@@ -50,6 +50,10 @@ CONFIGS = {
             chunks=1000, data=("hep", 64 * MiB), fmt="fp16"),
     3: dict(name="config3 hep-records 64 MiB, chunks_count=8192, d_model=256, num_layers=8", d=256, L=8,
             chunks=8192, data=("hep", 64 * MiB), fmt="fp16"),
+    4: dict(name="config4 records + CFD field 1 GiB, chunks_count=65536, d_model=512, num_layers=16, bf16",
+            d=512, L=16, chunks=65536, data=("mixed", 1 << 30), fmt="bf16"),
+    5: dict(name="config5 range coder only, 16384 streams x 65536 symbols, logits N(0, 3^2), BQ 2^16",
+            streams=16384, symbols=65536, slab=64),
 }
 
 
@@ -71,7 +75,15 @@ def make_data(cfg, size=None):
     from boa_b200 import synthetic
     kind, n = cfg["data"]
     n = size or n
-    return synthetic.markov(n, 1) if kind == "markov" else synthetic.hep_records(n, 2)
+    if kind == "markov":
+        return synthetic.markov(n, 1)
+    if kind == "mixed":
+        if n >= (1 << 30):
+            return synthetic.mixed(n, 3)
+        # a scaled-down config 4: the same records-then-field layout, 7/8 records
+        field = synthetic.cfd_field(256, (3, 1))[:n // 8]
+        return synthetic.hep_records(n - len(field), 3) + field
+    return synthetic.hep_records(n, 2)
 
 
 def chunk_array(data: bytes, n_chunks: int):
@@ -363,6 +375,150 @@ def run_ours(args, cfg, rank, world, local_rank, dist):
     }
     print(json.dumps(line), flush=True)
 
+# ---------------------------------------------------------------------------
+def _coder_slab(n_streams, n_steps, seed, device):
+    """Logits ~ N(0, 3^2) and symbols drawn from their softmax, [steps, streams]."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    logits = torch.randn((n_steps, n_streams, 256), generator=g, device=device) * 3.0
+    sym = torch.empty((n_steps, n_streams), dtype=torch.int32, device=device)
+    for i in range(n_steps):
+        sym[i] = torch.multinomial(torch.softmax(logits[i], -1), 1, generator=g).view(-1).to(torch.int32)
+    return logits, sym
+
+
+def coder_cpu_baseline(seconds_target=15.0):
+    """The CPU coder oracle (BQ quantiser, 2^16) on a bounded sample of config 5."""
+    import numpy as np
+    import torch
+    from oracle import orc
+    n, t = 64, 256
+    logits, sym = _coder_slab(n, t, 4, torch.device("cpu"))
+    rows = logits.permute(1, 0, 2).contiguous().numpy()
+    syms = sym.t().contiguous().numpy()
+    counts = np.full(n, t, np.int32)
+    pitch = (t * 16 + 31) // 32 + 8
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        w, sz, st = orc.encode(rows, syms, counts, 16, orc.MODE_BQ, pitch)
+        out = orc.decode(rows, w, sz, counts, 16, orc.MODE_BQ)
+        reps += 1
+        if time.perf_counter() - t0 > seconds_target / 3:
+            break
+    dt = time.perf_counter() - t0
+    assert st == 0 and np.array_equal(out, syms)
+    return {"value": reps * n * t / MiB / dt, "unit": "MiB/s", "cores": 1, "kind": "port",
+            "sample": f"{n} streams x {t} symbols, encode + decode, repeated {reps}x"}
+
+
+def run_coder(args, cfg, rank, world, local_rank, dist):
+    """Config 5: the range coder alone.  Each stream codes one symbol per step
+    from 256 fp32 logits (in-kernel BQ quantiser, total 2^16).  A slab of
+    `slab` steps of logits and symbols is generated on the device (untimed) and
+    cycled through; the per-step C-ABI calls (boa_rc_encode_step /
+    boa_rc_decode_step) are captured into one CUDA graph per slab pass."""
+    import ctypes
+    import numpy as np
+    import torch
+    import codec
+    from boa_b200 import _native as _n
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    N = cfg["streams"]
+    S = cfg["slab"]
+    T = max(S, ((args.size or cfg["symbols"]) // S) * S)
+    t0 = time.perf_counter()
+    logits, sym = _coder_slab(N, S, 4 + 1000 * rank, dev)
+    torch.cuda.synchronize(dev)
+    t_gen = time.perf_counter() - t0
+    pitch = codec.pitch_words_for(T + 1, 16)
+    lib = _n.load()
+
+    def one_round_trip(timed):
+        h = ctypes.c_void_p()
+        _n.call("boa_rc_create", ctypes.byref(h), N, 256, pitch, 16, _n.BOA_QUANT_BQ, local_rank)
+        try:
+            out = torch.empty((S, N), dtype=torch.int32, device=dev)
+            bad = torch.zeros((), dtype=torch.int64, device=dev)
+            ge, gd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(ge):
+                st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+                for i in range(S):
+                    _n.call("boa_rc_encode_step", h, ctypes.c_void_p(sym[i].data_ptr()),
+                            ctypes.c_void_p(logits[i].data_ptr()), None, st)
+            with torch.cuda.graph(gd):
+                st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+                for i in range(S):
+                    _n.call("boa_rc_decode_step", h, ctypes.c_void_p(logits[i].data_ptr()),
+                            ctypes.c_void_p(out[i].data_ptr()), None, st)
+                bad.add_((out != sym).sum())
+            stream = torch.cuda.current_stream(dev)
+            sp = ctypes.c_void_p(stream.cuda_stream)
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            if dist is not None:
+                dist.barrier()
+            torch.cuda.synchronize(dev)
+            e0.record(stream)
+            for _ in range(T // S):
+                ge.replay()
+            _n.call("boa_rc_finalize", h, sp)
+            e1.record(stream)
+            _n.call("boa_rc_init_decoder", h, sp)
+            for _ in range(T // S):
+                gd.replay()
+            e2.record(stream)
+            torch.cuda.synchronize(dev)
+            sizes = np.zeros(N, np.int32)
+            _n.call("boa_rc_get_sizes", h, sizes.ctypes.data_as(ctypes.c_void_p), sp)
+            if int(bad.item()) != 0:
+                raise RuntimeError("coder round trip mismatch")
+            del ge, gd
+            return e0.elapsed_time(e1) / 1000.0, e1.elapsed_time(e2) / 1000.0, int(sizes.astype(np.int64).sum())
+        finally:
+            lib.boa_rc_destroy(h)
+
+    for _ in range(max(args.warmup, 1)):
+        one_round_trip(False)
+    te = td = 0.0
+    words = 0
+    with ClockSampler(local_rank) as clk:
+        for _ in range(args.steps):
+            a_, b_, words = one_round_trip(True)
+            te += a_
+            td += b_
+    tt = torch.tensor([te + td, te, td], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t_tot, te, td = (float(x) for x in tt.cpu())
+    if rank != 0:
+        return
+    syms_total = N * T
+    peak, peak_src = measured_peak()
+    code_bytes = 4.0 * words / syms_total
+    per_sym = 256 * 4 + 4 + 64 + code_bytes
+    ach = per_sym * N / (td / args.steps / T) / 1e9
+    roof = {"bound": "hbm", "kernel": "k_rc_decode_bq (one decode step of 16384 streams)",
+            "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "peak_source": peak_src,
+            "traffic": None, "algorithmic_bytes_per_launch": per_sym * N,
+            "per_unit": "1024 B fp32 logits + 4 B symbol + 64 B coder state read+write + code bytes per symbol"}
+    line = {
+        "metric": "range-coder encode+decode round-trip throughput", "value": world * args.steps * syms_total / MiB / t_tot,
+        "unit": "MiB/s (1 symbol = 1 byte)", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * t_tot / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 logits, u32 coder", "data": "synthetic (seeded N(0, 3^2) logits, symbols "
+        "drawn from their softmax)",
+        "config": {"workload": cfg["name"], "streams_per_gpu": N, "symbols_per_stream": T, "slab_steps": S,
+                   "slab_generation_s": t_gen, "l2": "inputs larger than L2: logits slab %d MB" % (S * N * 1024 // 1000000)},
+        "encode_Msym_per_s": world * args.steps * syms_total / 1e6 / te,
+        "decode_Msym_per_s": world * args.steps * syms_total / 1e6 / td,
+        "bits_per_symbol": 32.0 * words / syms_total,
+        "roofline": roof, "cpu_baseline": (coder_cpu_baseline() if world == 1 and not args.no_cpu_baseline else None),
+        "e2e": None, "clocks": clk.summary(), "gpu_launches": args.steps * (2 * T + 2),
+    }
+    print(json.dumps(line), flush=True)
+
 
 def main():
     args = parse()
@@ -371,6 +527,18 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
+        if args.config == 5:
+            if rank == 0:
+                cb = coder_cpu_baseline()
+                print(json.dumps({"impl": "reference", "metric": "range-coder encode+decode round-trip throughput",
+                                  "value": cb["value"], "unit": "MiB/s (1 symbol = 1 byte)", "n_gpus": world,
+                                  "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                                  "scaling": "weak", "vs_baseline": None, "dtype": "f32 logits, u32 coder",
+                                  "data": "synthetic", "config": {"workload": cfg["name"], "sample": cb["sample"]},
+                                  "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "MiB/s",
+                                                              "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+                      flush=True)
+            return
         run_reference(args, cfg, rank)
         return
     dist = None
@@ -383,7 +551,10 @@ def main():
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
         dist = tdist
     try:
-        run_ours(args, cfg, rank, world, local_rank, dist)
+        if args.config == 5:
+            run_coder(args, cfg, rank, world, local_rank, dist)
+        else:
+            run_ours(args, cfg, rank, world, local_rank, dist)
     finally:
         if dist is not None:
             dist.destroy_process_group()
