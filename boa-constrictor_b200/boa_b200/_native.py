@@ -50,6 +50,8 @@ SIGNATURES = {
     "boa_rc_finalize": [_P, _P],
     "boa_rc_init_decoder": [_P, _P],
     "boa_rc_decode_step": [_P, _P, _P, _P, _P],
+    "boa_rc_encode_steps": [_P, _I, _I, _P, _I64, _P, _I64, _P, _I64, _P],
+    "boa_rc_decode_steps": [_P, _I, _I, _P, _I64, _P, _I64, _P, _I64, _P],
     "boa_rc_encode_noalloc": [_I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P],
     "boa_model_create": [_P, _I, _I, _I, _P, _SZ, _I, _I],
     "boa_model_destroy": [_P],

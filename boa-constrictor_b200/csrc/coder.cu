@@ -150,6 +150,109 @@ __global__ void __launch_bounds__(256) k_rc_decode_bq(int n, int K, int precisio
   }
 }
 
+
+// Multi-step BQ coder: one warp per stream codes n_steps symbols in one
+// launch, the coder state in registers of lane 0 and the next step's logits
+// row loaded while the current one is coded.  Step t reads row / symbol / mask
+// slot (t % period) (period <= 0: slot t) at the given per-slot strides.
+template <int Q>
+__device__ __forceinline__ void rc_load_row(float (&v)[Q], const float* __restrict__ row, int K, int lane) {
+  if (Q % 4 == 0 && K == 32 * Q) {
+#pragma unroll
+    for (int q = 0; q < Q; q += 4) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(row + lane * Q + q));
+      v[q] = t.x; v[q + 1] = t.y; v[q + 2] = t.z; v[q + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+      const int idx = lane * Q + q;
+      v[q] = idx < K ? __ldg(row + idx) : 0.0f;
+    }
+  }
+}
+
+template <int Q>
+__global__ void __launch_bounds__(256) k_rc_encode_bq_steps(int n, int K, int precision, int n_steps, int period,
+                                                            const float* __restrict__ logits, long long row_stride,
+                                                            const int32_t* __restrict__ syms, long long sym_stride,
+                                                            const uint8_t* __restrict__ mask, long long mask_stride,
+                                                            RcEnc* __restrict__ enc, uint32_t* __restrict__ words,
+                                                            int pitch, uint32_t* err) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < n; i += warps) {
+    RcEnc st = enc[i];
+    uint32_t* wrow = words + (size_t)i * (size_t)pitch;
+    float v[Q];
+    rc_load_row<Q>(v, logits + (size_t)i * (size_t)K, K, lane);
+    int slot = 0;
+    for (int t = 0; t < n_steps; ++t) {
+      const int next = (period > 0 && slot + 1 == period) ? 0 : slot + 1;
+      float nv[Q];
+      if (t + 1 < n_steps) rc_load_row<Q>(nv, logits + (long long)next * row_stride + (size_t)i * (size_t)K, K, lane);
+      const bool on = !mask || mask[(long long)slot * mask_stride + i] != 0;
+      const int s = syms[(long long)slot * sym_stride + i];
+      if (on && (s < 0 || s >= K)) {
+        if (lane == 0) atomicOr(err, RC_ERR_SYMBOL);
+      } else if (on) {
+        uint32_t f[Q], base;
+        bq_quantise_warp<Q>(v, K, precision, lane, f, base);
+        uint32_t left, freq;
+        bq_lookup_warp<Q>(f, base, s, lane, left, freq);
+        if (lane == 0) rc_enc_put(st, left, freq, precision, wrow, pitch, err);
+      }
+      if (t + 1 < n_steps) {
+#pragma unroll
+        for (int q = 0; q < Q; ++q) v[q] = nv[q];
+      }
+      slot = next;
+    }
+    if (lane == 0) enc[i] = st;
+  }
+}
+
+template <int Q>
+__global__ void __launch_bounds__(256) k_rc_decode_bq_steps(int n, int K, int precision, int n_steps, int period,
+                                                            const float* __restrict__ logits, long long row_stride,
+                                                            const uint8_t* __restrict__ mask, long long mask_stride,
+                                                            RcDec* __restrict__ dec, const uint32_t* __restrict__ words,
+                                                            int pitch, const int32_t* __restrict__ sizes,
+                                                            int32_t* __restrict__ out, long long out_stride) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < n; i += warps) {
+    RcDec d = dec[i];
+    const uint32_t* wrow = words + (size_t)i * (size_t)pitch;
+    int nw = sizes[i];
+    nw = nw < 0 ? 0 : (nw > pitch ? pitch : nw);
+    float v[Q];
+    rc_load_row<Q>(v, logits + (size_t)i * (size_t)K, K, lane);
+    int slot = 0;
+    for (int t = 0; t < n_steps; ++t) {
+      const int next = (period > 0 && slot + 1 == period) ? 0 : slot + 1;
+      float nv[Q];
+      if (t + 1 < n_steps) rc_load_row<Q>(nv, logits + (long long)next * row_stride + (size_t)i * (size_t)K, K, lane);
+      if (!mask || mask[(long long)slot * mask_stride + i] != 0) {
+        uint32_t f[Q], base;
+        bq_quantise_warp<Q>(v, K, precision, lane, f, base);
+        unsigned long long scale;
+        const uint32_t target = rc_dec_target(d, precision, scale);
+        uint32_t left, freq;
+        const int s = bq_search_warp<Q>(f, base, target, lane, left, freq);
+        rc_dec_advance(d, scale, left, freq, wrow, nw);     // every lane: the state stays warp-uniform
+        if (lane == 0) out[(long long)slot * out_stride + i] = s;
+      }
+      if (t + 1 < n_steps) {
+#pragma unroll
+        for (int q = 0; q < Q; ++q) v[q] = nv[q];
+      }
+      slot = next;
+    }
+    if (lane == 0) dec[i] = d;
+  }
+}
+
 __global__ void __launch_bounds__(128) k_rc_decode_ref(int n, int K, int precision, const float* __restrict__ probs,
                                                        const uint8_t* __restrict__ mask, RcDec* __restrict__ dec,
                                                        const uint32_t* __restrict__ words, int pitch,
@@ -360,6 +463,50 @@ BOA_API int boa_rc_decode_step(boa_rc_batch* b, const float* d_rows, int32_t* d_
     k_rc_decode_ref<<<(b->n + 127) / 128, 128, 0, s>>>(b->n, b->K, b->precision, d_rows, d_mask, b->dec,
                                                        b->words, b->pitch, b->sizes, d_out_symbols);
   }
+  BOA_CUDA(cudaGetLastError());
+  return BOA_OK;
+}
+
+BOA_API int boa_rc_encode_steps(boa_rc_batch* b, int n_steps, int period, const int32_t* d_symbols,
+                                int64_t sym_stride, const float* d_rows, int64_t row_stride, const uint8_t* d_mask,
+                                int64_t mask_stride, void* stream) {
+  if (!b || !d_symbols || !d_rows || n_steps < 0) return boa_fail(BOA_ERR_ARG, "boa_rc_encode_steps: bad argument");
+  if (b->quantiser != BOA_QUANT_BQ)
+    return boa_fail(BOA_ERR_UNSUPPORTED, "boa_rc_encode_steps: BOA_QUANT_BQ handles only");
+  if (n_steps == 0) return BOA_OK;
+  BOA_CUDA(cudaSetDevice(b->device));
+  cudaStream_t s = (cudaStream_t)stream;
+  const int grid = rc_grid_warps(b->n);
+  if (b->K <= 256)
+    k_rc_encode_bq_steps<8><<<grid, 256, 0, s>>>(b->n, b->K, b->precision, n_steps, period, d_rows, row_stride,
+                                                 d_symbols, sym_stride, d_mask, mask_stride, b->enc, b->words,
+                                                 b->pitch, b->err);
+  else
+    k_rc_encode_bq_steps<32><<<grid, 256, 0, s>>>(b->n, b->K, b->precision, n_steps, period, d_rows, row_stride,
+                                                  d_symbols, sym_stride, d_mask, mask_stride, b->enc, b->words,
+                                                  b->pitch, b->err);
+  BOA_CUDA(cudaGetLastError());
+  return BOA_OK;
+}
+
+BOA_API int boa_rc_decode_steps(boa_rc_batch* b, int n_steps, int period, const float* d_rows, int64_t row_stride,
+                                int32_t* d_out_symbols, int64_t out_stride, const uint8_t* d_mask,
+                                int64_t mask_stride, void* stream) {
+  if (!b || !d_rows || !d_out_symbols || n_steps < 0) return boa_fail(BOA_ERR_ARG, "boa_rc_decode_steps: bad argument");
+  if (b->quantiser != BOA_QUANT_BQ)
+    return boa_fail(BOA_ERR_UNSUPPORTED, "boa_rc_decode_steps: BOA_QUANT_BQ handles only");
+  if (n_steps == 0) return BOA_OK;
+  BOA_CUDA(cudaSetDevice(b->device));
+  cudaStream_t s = (cudaStream_t)stream;
+  const int grid = rc_grid_warps(b->n);
+  if (b->K <= 256)
+    k_rc_decode_bq_steps<8><<<grid, 256, 0, s>>>(b->n, b->K, b->precision, n_steps, period, d_rows, row_stride,
+                                                 d_mask, mask_stride, b->dec, b->words, b->pitch, b->sizes,
+                                                 d_out_symbols, out_stride);
+  else
+    k_rc_decode_bq_steps<32><<<grid, 256, 0, s>>>(b->n, b->K, b->precision, n_steps, period, d_rows, row_stride,
+                                                  d_mask, mask_stride, b->dec, b->words, b->pitch, b->sizes,
+                                                  d_out_symbols, out_stride);
   BOA_CUDA(cudaGetLastError());
   return BOA_OK;
 }

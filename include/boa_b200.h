@@ -94,6 +94,22 @@ BOA_API int boa_rc_init_decoder(boa_rc_batch* b, void* stream);
 BOA_API int boa_rc_decode_step(boa_rc_batch* b, const float* d_rows, int32_t* d_out_symbols,
                                const uint8_t* d_mask, void* stream);
 
+/* Multi-step forms of encode_step / decode_step (no counterpart in the
+ * reference, which launches once per symbol, gpu_range_coder.py:265-305):
+ * one launch codes n_steps symbols per stream, the coder state held in
+ * registers across the steps.  Step t uses slot (t % period) of each per-step
+ * array (period <= 0: slot t): rows at d_rows + slot * row_stride ([n, K]
+ * fp32 logits), symbols at d_symbols + slot * sym_stride (encode), outputs at
+ * d_out_symbols + slot * out_stride (decode), mask bytes at d_mask + slot *
+ * mask_stride (NULL: every stream codes every step).  Strides are in
+ * elements.  Same bits as n_steps single-step calls.  BOA_QUANT_BQ only. */
+BOA_API int boa_rc_encode_steps(boa_rc_batch* b, int n_steps, int period, const int32_t* d_symbols,
+                                int64_t sym_stride, const float* d_rows, int64_t row_stride, const uint8_t* d_mask,
+                                int64_t mask_stride, void* stream);
+BOA_API int boa_rc_decode_steps(boa_rc_batch* b, int n_steps, int period, const float* d_rows, int64_t row_stride,
+                                int32_t* d_out_symbols, int64_t out_stride, const uint8_t* d_mask,
+                                int64_t mask_stride, void* stream);
+
 /* Allocation-free whole-stream encode (no counterpart in the reference).
  * For callers that cannot allocate device memory while they code (work being
  * captured into a CUDA graph, hosts that forbid allocation after start-up):

@@ -80,3 +80,60 @@ def test_many_streams_bq():
     ow, osz, st = orc.encode(rows, syms, counts, 16, orc.MODE_BQ, 2 * T + 8)
     comp = _gpu_encode(rows, syms, counts, 16, "bq", 2 * T + 8)
     assert all(np.array_equal(comp[i], ow[i, :osz[i]]) for i in range(N))
+
+
+@pytest.mark.parametrize("K,period", [(256, 0), (256, 24), (200, 7)])
+def test_multi_step_entry_points_match_single_steps(K, period):
+    """boa_rc_encode_steps / decode_steps (one launch for many steps, slots
+    reused every `period` steps) write the words the oracle writes for the
+    same step sequence, and decode it back."""
+    import ctypes
+    from boa_b200 import _native as _n
+    N, T = 45, 80
+    P = period if period > 0 else T
+    rows, syms, _ = make_case(7 + K + period, N, P, K, orc.MODE_BQ, 16)
+    rng = np.random.default_rng(period + 1)
+    mask = (rng.random((P, N)) > 0.2).astype(np.uint8)
+    slot = np.array([t % P for t in range(T)])
+    # the equivalent step sequence for the oracle: masked steps are skipped
+    full_rows = rows[:, slot]                        # [N, T, K]
+    full_syms = syms[:, slot]
+    keep = mask[slot].T.astype(bool)                 # [N, T]
+    counts = keep.sum(1).astype(np.int32)
+    o_rows = np.zeros_like(full_rows)
+    o_syms = np.zeros_like(full_syms)
+    for i in range(N):
+        o_rows[i, :counts[i]] = full_rows[i, keep[i]]
+        o_syms[i, :counts[i]] = full_syms[i, keep[i]]
+    pitch = T // 2 + 16
+    ow, osz, st = orc.encode(o_rows, o_syms, counts, 16, orc.MODE_BQ, pitch)
+    assert st == 0
+    R = torch.from_numpy(np.ascontiguousarray(rows.transpose(1, 0, 2))).cuda()     # [P, N, K]
+    S = torch.from_numpy(np.ascontiguousarray(syms.T)).cuda()                      # [P, N]
+    M = torch.from_numpy(mask).cuda()
+    h = ctypes.c_void_p()
+    _n.call("boa_rc_create", ctypes.byref(h), N, K, pitch, 16, _n.BOA_QUANT_BQ, 0)
+    try:
+        sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        _n.call("boa_rc_encode_steps", h, T, period, ctypes.c_void_p(S.data_ptr()), N,
+                ctypes.c_void_p(R.data_ptr()), N * K, ctypes.c_void_p(M.data_ptr()), N, sp)
+        _n.call("boa_rc_finalize", h, sp)
+        words = np.zeros((N, pitch), np.uint32)
+        sizes = np.zeros(N, np.int32)
+        _n.call("boa_rc_get_sizes", h, sizes.ctypes.data_as(ctypes.c_void_p), sp)
+        _n.call("boa_rc_get_words", h, words.ctypes.data_as(ctypes.c_void_p), sp)
+        assert np.array_equal(sizes, osz)
+        for i in range(N):
+            assert np.array_equal(words[i, :sizes[i]], ow[i, :osz[i]]), i
+        _n.call("boa_rc_init_decoder", h, sp)
+        out = torch.full((T, N), -1, dtype=torch.int32, device="cuda")
+        # decode with the same slot layout, one output row per step
+        Rf = torch.from_numpy(np.ascontiguousarray(full_rows.transpose(1, 0, 2))).cuda()   # [T, N, K]
+        Mf = torch.from_numpy(np.ascontiguousarray(mask[slot])).cuda()                    # [T, N]
+        _n.call("boa_rc_decode_steps", h, T, 0, ctypes.c_void_p(Rf.data_ptr()), N * K,
+                ctypes.c_void_p(out.data_ptr()), N, ctypes.c_void_p(Mf.data_ptr()), N, sp)
+        got = out.cpu().numpy().T                                                          # [N, T]
+        for i in range(N):
+            assert np.array_equal(got[i, keep[i]], full_syms[i, keep[i]]), i
+    finally:
+        _n.load().boa_rc_destroy(h)
