@@ -201,6 +201,11 @@ __device__ __forceinline__ uint32_t peer_addr(const void* local, uint32_t peer) 
 __device__ __forceinline__ void st_cluster_b16(uint32_t addr, unsigned short v) {
   asm volatile("st.shared::cluster.b16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
 }
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
 __device__ __forceinline__ void st_cluster_b32(uint32_t addr, uint32_t v) {
   asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
@@ -524,24 +529,31 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
 #endif
     // operand buffer the next GEMM reads
     auto bnext = [&]() -> uint8_t* { return bbuf0 + (gemm_no % S::NBUF) * S::BBUF; };
-    // write one operand element of the next GEMM, also into the peer when `share`
-    auto put_b = [&](uint8_t* buf, int n, int k, float v, bool share) {
-      const uint32_t off = tc::sw128_offset<KIND>(n, k, CT);
-      tc::store_operand<KIND>(buf, n, k, CT, v);
+    // write one operand element of the next GEMM (this CTA's copy)
+    auto put_b = [&](uint8_t* buf, int n, int k, float v) { tc::store_operand<KIND>(buf, n, k, CT, v); };
+    // SPLIT == 2: after all threads wrote this CTA's share of the next operand
+    // (K slices [s0, s0 + ns), contiguous in the buffer), copy it into the
+    // peer's buffer, 16 bytes per thread and store
+    auto push_slices = [&](uint8_t* buf, int s0, int ns) {
       if constexpr (SPLIT == 2) {
-        if (share) {
-          const uint32_t raddr = peer_bbuf + (uint32_t)(buf - bbuf0) + off;
-          if constexpr (KIND == 0) {
-            st_cluster_b32(raddr, *reinterpret_cast<const uint32_t*>(buf + off));
-          } else {
-            st_cluster_b16(raddr, *reinterpret_cast<const unsigned short*>(buf + off));
-          }
-        }
+        cbar_sync();
+        const uint32_t off0 = (uint32_t)(buf - bbuf0) + (uint32_t)(s0 * CT * 128);
+        const int bytes = ns * CT * 128;
+        for (int o = ct * 16; o < bytes; o += kComputeThreads * 16)
+          st_cluster_v4(peer_bbuf + off0 + (uint32_t)o, *reinterpret_cast<const uint4*>(bbuf0 + off0 + o));
       }
     };
-    auto put_f32 = [&](float* arr, uint32_t peer_arr, int idx, float v) {
-      arr[idx] = v;
-      if constexpr (SPLIT == 2) st_cluster_b32(peer_arr + 4u * (uint32_t)idx, __float_as_uint(v));
+    // SPLIT == 2: copy columns [c, c + nf) of the CT rows of an fp32 [CT][row] array into the peer
+    auto push_rows = [&](float* arr, uint32_t peer_arr, int row, int c, int nf) {
+      if constexpr (SPLIT == 2) {
+        cbar_sync();
+        const int per_row = nf / 4;
+        for (int i = ct; i < CT * per_row; i += kComputeThreads) {
+          const int r = i / per_row;
+          const int idx = r * row + c + 4 * (i - r * per_row);
+          st_cluster_v4(peer_arr + 4u * (uint32_t)idx, *reinterpret_cast<const uint4*>(arr + idx));
+        }
+      }
     };
     // Every thread orders its operand writes (and TMEM reads) before the
     // warp barrier; lane 0 then arrives once for the warp, which keeps the
@@ -665,13 +677,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
                 const float xc = silu_fast(acc);
                 win = make_float4(win.y, win.z, xv[j], 0.f);
                 if ((smask >> n) & 1u) cs[(n / TB) * cst] = win;
-                put_b(buf, n, e, xc, true);
+                put_b(buf, n, e, xc);
                 xv[j] = xc;
               }
               tc::tmem_st8(tq + col, xv);
             }
           }
           tc::tmem_wait_st();
+          push_slices(buf, (int)rank * (LT_E * 128 / PER), LT_E * 128 / PER);   // xc: x_proj runs whole
         }
         arrive_act();
         mark(PF_CONV);
@@ -708,6 +721,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
             const int lt = u / RUNS, n0 = (u % RUNS) * RUN;
             const int e = (int)(rank * LT_E + lt) * 128 + row;
             const float4* A2p = reinterpret_cast<const float4*>(lp + LP::A2) + e * 4;
+            // time blocks run 4x the columns per channel: keep A in registers there
+            float4 Areg[TB > 1 ? 4 : 1];
+            if constexpr (TB > 1) {
+#pragma unroll
+              for (int k = 0; k < 4; ++k) Areg[k] = __ldg(A2p + k);
+            }
             const float Dp = __ldg(lp + LP::Dp + e);
             const float bdt = __ldg(lp + LP::dtb + e);
             // SSM state layout [chunk][layer][k = 0..3][channel] of float4: a
@@ -747,7 +766,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
                 float y = 0.f;
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                  const float4 A4 = __ldg(A2p + k);
+                  float4 A4;
+                  if constexpr (TB > 1) A4 = Areg[k];
+                  else A4 = __ldg(A2p + k);
                   const float4 B4 = bc4[k];
                   const float4 C4 = bc4[4 + k];
                   h[4 * k + 0] = fmaf(h[4 * k + 0], ex2_approx(dtv * A4.x), dx * B4.x);
@@ -766,10 +787,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
                 }
                 y = fmaf(Dp, xc[j], y);
                 y *= silu_fast(z[j]);
-                put_b(buf, n, e, y, true);
+                put_b(buf, n, e, y);
               }
             }
           }
+          push_slices(buf, (int)rank * (LT_E * 128 / PER), LT_E * 128 / PER);
         }
         arrive_act();
         mark(PF_SCAN);
@@ -783,9 +805,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
           tc::tmem_ld8(tq + (uint32_t)(lt * CT + 8 * gi), v);
           if (f < D) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) put_f32(scr, peer_scr, (8 * gi + j) * D + f, v[j]);
+            for (int j = 0; j < 8; ++j) scr[(8 * gi + j) * D + f] = v[j];
           }
         }
+        push_rows(scr, peer_scr, D, (int)rank * LT_D * 128, LT_D * 128);
         if (!(ok = exchange())) break;
         layernorm_to_b(scr, lp + LP::ln2w, lp + LP::ln2b);
         arrive_act();
@@ -802,8 +825,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
             float v[8];
             tc::tmem_ld8(tq + (uint32_t)(lt * CT + 8 * gi), v);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) put_b(buf, 8 * gi + j, f, gelu_f(v[j] + b), true);
+            for (int j = 0; j < 8; ++j) put_b(buf, 8 * gi + j, f, gelu_f(v[j] + b));
           }
+          push_slices(buf, (int)rank * (LT_F * 128 / PER), LT_F * 128 / PER);
         }
         arrive_act();
         mark(PF_FF1);
@@ -820,10 +844,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               const int idx = (8 * gi + j) * D + f;
-              put_f32(hres, peer_hres, idx, hres[idx] + v[j] + b);
+              hres[idx] = hres[idx] + v[j] + b;
             }
           }
         }
+        push_rows(hres, peer_hres, D, (int)rank * LT_D * 128, LT_D * 128);
         if (!(ok = exchange())) break;
         mark(PF_FF2);
       }
@@ -850,9 +875,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
           if (f < D) {
             const float b = __ldg(P + o_bh0 + f);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) put_b(buf, 8 * gi + j, f, fmaxf(v[j] + b, 0.f), true);
+            for (int j = 0; j < 8; ++j) put_b(buf, 8 * gi + j, f, fmaxf(v[j] + b, 0.f));
           }
         }
+        push_slices(buf, (int)rank * (LT_D * 128 / PER), LT_D * 128 / PER);
       }
       arrive_act();
       mark(PF_HEAD1);
@@ -866,8 +892,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         float v[8];
         tc::tmem_ld8(tq + (uint32_t)(lt * CT + 8 * gi), v);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) put_f32(scr, peer_scr, (8 * gi + j) * 256 + vv, v[j] + b);
+        for (int j = 0; j < 8; ++j) scr[(8 * gi + j) * 256 + vv] = v[j] + b;
       }
+      push_rows(scr, peer_scr, 256, (int)rank * LT_V * 128, LT_V * 128);
       if (!(ok = exchange())) break;
       mark(PF_HEAD2);
       // ---- quantiser + range coder, a warp per chunk (both CTAs, identical);
