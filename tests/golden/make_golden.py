@@ -17,6 +17,10 @@ Fixtures:
       oracle logits (computed in fp64, stored fp32) of that model for 3 streams x 24 seeded tokens.
   synthetic.json
       sha256 of the config-1 input and of the first 1 MiB of the config-2 input.
+  bq_tables.npz
+      seeded logit rows (wide, narrow, near-deterministic, NaN, +inf, K = 256
+      and K = 37) and their BQ integer-quantiser CDFs at totals 2^16 and 2^24
+      from the C oracle: pins this build's quantiser definition.
 """
 from __future__ import annotations
 
@@ -34,6 +38,28 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(ROOT, "boa-constrictor_b200"))
 sys.path.insert(0, ROOT)
+
+
+def bq_rows():
+    rng = np.random.default_rng(77)
+    rows = [rng.normal(0, 3, 256), rng.normal(0, 0.1, 256), rng.normal(-30, 1, 256)]
+    rows[2][5] = 30.0                                  # one dominant entry: many frequency-1 symbols
+    nan_row = rng.normal(0, 1, 256)
+    nan_row[17] = np.nan                               # degenerate: uniform table
+    inf_row = rng.normal(0, 1, 256)
+    inf_row[3] = np.inf
+    rows += [nan_row, inf_row]
+    return np.asarray(rows, np.float32), rng.normal(0, 2, 37).astype(np.float32)
+
+
+def write_bq_tables():
+    from oracle import orc
+    rows, row37 = bq_rows()
+    out = {"rows": rows, "row37": row37}
+    for P in (16, 24):
+        out[f"cdf{P}"] = np.stack([orc.cdf_bq(r, P) for r in rows])
+        out[f"cdf37_{P}"] = orc.cdf_bq(row37, P)
+    np.savez_compressed(os.path.join(HERE, "bq_tables.npz"), **out)
 
 
 def container_case():
@@ -59,7 +85,11 @@ class BoaBytePredictor(torch.nn.Module):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only-bq", action="store_true", help="write bq_tables.npz only (no reference tree needed)")
     a = ap.parse_args()
+    if a.only_bq:
+        write_bq_tables()
+        return
     from boa_b200 import container as C
     from model import seeded_model
     from boa_b200 import synthetic
@@ -123,6 +153,7 @@ def main():
     with open(os.path.join(HERE, "synthetic.json"), "w") as f:
         json.dump({"config1_sha256": hashlib.sha256(d1).hexdigest(), "config1_len": len(d1),
                    "hep_1MiB_seed2_sha256": hashlib.sha256(d2).hexdigest()}, f, indent=1)
+    write_bq_tables()
     print("golden fixtures written to", HERE)
 
 

@@ -137,3 +137,23 @@ def test_multi_step_entry_points_match_single_steps(K, period):
             assert np.array_equal(got[i, keep[i]], full_syms[i, keep[i]]), i
     finally:
         _n.load().boa_rc_destroy(h)
+
+
+@pytest.mark.parametrize("precision", [16, 24])
+def test_gpu_coder_on_golden_quantiser_rows(precision):
+    """The GPU coder, fed the committed golden logit rows (including NaN and
+    +inf rows, which fall back to the uniform table), writes the bitstream the
+    oracle writes from the committed tables."""
+    import os
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "bq_tables.npz"))
+    base = z["rows"]                                           # [5, 256]
+    N, T = base.shape[0], 64
+    rows = np.repeat(base[:, None, :], T, axis=1)              # [N, T, 256]
+    syms = ((np.arange(T)[None, :] * 7 + np.arange(N)[:, None] * 31) % 256).astype(np.int32)
+    counts = np.full(N, T, np.int32)
+    pitch = (T * precision + 31) // 32 + 8
+    ow, osz, st = orc.encode(rows, syms, counts, precision, orc.MODE_BQ, pitch)
+    assert st == 0
+    comp = _gpu_encode(rows, syms, counts, precision, "bq", pitch)
+    for i in range(N):
+        assert np.array_equal(comp[i], ow[i, :osz[i]]), i

@@ -107,3 +107,17 @@ def test_hep_record_structure():
             pos += 14
         ev += 1
     assert ev > 300
+
+
+def test_bq_quantiser_matches_golden_tables():
+    """The C oracle's integer quantiser reproduces the committed tables
+    (wide / narrow / near-deterministic / NaN / +inf rows, K = 256 and 37,
+    totals 2^16 and 2^24)."""
+    from oracle import orc
+    z = np.load(os.path.join(G, "bq_tables.npz"))
+    for P in (16, 24):
+        for r in range(z["rows"].shape[0]):
+            assert np.array_equal(orc.cdf_bq(z["rows"][r], P), z[f"cdf{P}"][r]), (P, r)
+        assert np.array_equal(orc.cdf_bq(z["row37"], P), z[f"cdf37_{P}"]), P
+    c = z["cdf16"]
+    assert np.all(c[:, -1] == 1 << 16) and np.all(np.diff(c.astype(np.int64), axis=1) >= 1)

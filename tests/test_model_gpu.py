@@ -101,3 +101,24 @@ def test_logits_identical_across_decompositions(fmt):
     assert torch.equal(small, got_big)
     assert torch.equal(small, got_tb)
     assert torch.equal(small, got_tb_mid)
+
+
+def test_evaluate_bpp_matches_oracle():
+    """train.evaluate_bpp through the native forward equals the bits per byte
+    of the fp64 oracle's logits on the same batches."""
+    import math
+    from model import seeded_model
+    from train import evaluate_bpp
+    m = seeded_model(64, 2)
+    rng = np.random.default_rng(12)
+    batches = [torch.from_numpy(rng.integers(0, 256, (6, 33)).astype(np.int64)) for _ in range(3)]
+    got = evaluate_bpp(m, batches, torch.nn.CrossEntropyLoss(), device="cuda")
+    sd = {k: v.detach().float() for k, v in m.state_dict().items()}
+    cfg = mo.config_from_state_dict(sd)
+    tot, n = 0.0, 0
+    for b in batches:
+        lg = mo.forward(sd, cfg, b[:, :-1], dtype=torch.float64)
+        tot += torch.nn.functional.cross_entropy(lg.reshape(-1, 256), b[:, 1:].reshape(-1), reduction="sum").item()
+        n += b[:, 1:].numel()
+    ref = tot / n / math.log(2.0)
+    assert abs(got - ref) < 1e-4 * ref, (got, ref)
