@@ -87,8 +87,30 @@ def BOA(device, filepath: str, model):
         def get_metadata(self):
             return dict(self.metadata)
 
+        def _encode_wave(self, mm, lens, chunk_len, b0, b1):
+            """Code chunks [b0, b1): (first bytes, per-chunk little-endian u32 payloads)."""
+            nb = b1 - b0
+            maxL = max(lens[b0:b1])
+            host = torch.zeros((nb, maxL), dtype=torch.uint8, pin_memory=True)
+            hv = host.numpy()
+            for j, i in enumerate(range(b0, b1)):
+                s = i * chunk_len
+                hv[j, :lens[i]] = mm[s:s + lens[i]]
+            X = host.to(dev, non_blocking=True)
+            L_d = torch.tensor(lens[b0:b1], dtype=torch.int32).to(dev, non_blocking=True)
+            words, sizes = _codec.encode_device(self.model, X, L_d, precision=self.precision)
+            sz = sizes.cpu().numpy().astype(np.int64)
+            wh = words.cpu().numpy().view(np.uint32)
+            return hv[:, 0].astype(np.int64), [wh[j, :sz[j]].astype("<u4").tobytes() for j in range(nb)]
+
         # ------------------------------------------------------------------
-        def compress(self, data_path: str, seq_size: int = 0, chunks_count: int = 0, progress: bool = True):
+        def compress(self, data_path: str, seq_size: int = 0, chunks_count: int = 0, progress: bool = True,
+                     resume: bool = False):
+            """boa.py:159-268.  One process: every wave's payload is appended to
+            the file as soon as it is coded (StreamingWriter); with resume=True a
+            run that stopped between waves continues after the last complete
+            wave.  Several ranks: each codes its contiguous chunk range and
+            writes its payload at the gathered offsets."""
             p = Path(data_path)
             total = p.stat().st_size
             if total <= 0:
@@ -104,29 +126,34 @@ def BOA(device, filepath: str, model):
             lo, hi = shard_range(n_chunks, world, rank)
             mm = np.memmap(p, dtype=np.uint8, mode="r")
             stream_n = self._gpu_streams(max(hi - lo, 1))
+            hdr = C.header_bytes(C.make_flags(self.precision), total, chunk_len, n_chunks, last,
+                                 self._model_fingerprint())
+            if dist is None:
+                w = C.StreamingWriter(self.filepath, hdr, n_chunks, resume=resume)
+                try:
+                    for b0 in range(w.chunks_done, n_chunks, stream_n):
+                        b1 = min(b0 + stream_n, n_chunks)
+                        firsts, payload = self._encode_wave(mm, lens, chunk_len, b0, b1)
+                        w.append(firsts, payload)
+                    w.finish()
+                finally:
+                    w.close()
+                self.compressed_data = []
+                self.first_bytes = list(w.firsts)
+                self.lengths = lens
+                if progress:
+                    print(f"Compression complete: {n_chunks} chunks, chunk_len={chunk_len}, last={last}")
+                return
             sizes_local = np.zeros(hi - lo, dtype=np.int64)
             firsts_local = np.zeros(hi - lo, dtype=np.int64)
             payloads = []
             for b0 in range(lo, hi, stream_n):
                 b1 = min(b0 + stream_n, hi)
-                nb = b1 - b0
-                maxL = max(lens[b0:b1])
-                host = torch.zeros((nb, maxL), dtype=torch.uint8, pin_memory=True)
-                hv = host.numpy()
-                for j, i in enumerate(range(b0, b1)):
-                    s = i * chunk_len
-                    hv[j, :lens[i]] = mm[s:s + lens[i]]
-                firsts_local[b0 - lo:b1 - lo] = hv[:, 0]
-                X = host.to(dev, non_blocking=True)
-                L_d = torch.tensor(lens[b0:b1], dtype=torch.int32).to(dev, non_blocking=True)
-                words, sizes = _codec.encode_device(self.model, X, L_d, precision=self.precision)
-                sz = sizes.cpu().numpy().astype(np.int64)
-                wh = words.cpu().numpy().view(np.uint32)
-                sizes_local[b0 - lo:b1 - lo] = 4 * sz
-                payloads.append(b"".join(wh[j, :sz[j]].astype("<u4").tobytes() for j in range(nb)))
+                firsts, payload = self._encode_wave(mm, lens, chunk_len, b0, b1)
+                firsts_local[b0 - lo:b1 - lo] = firsts
+                sizes_local[b0 - lo:b1 - lo] = [len(x) for x in payload]
+                payloads.append(b"".join(payload))
             sizes_bytes, firsts = gather_lengths(dist, n_chunks, lo, hi, sizes_local, firsts_local)
-            hdr = C.header_bytes(C.make_flags(self.precision), total, chunk_len, n_chunks, last,
-                                 self._model_fingerprint())
             write_sharded(self.filepath, hdr, lambda offs: C.index_bytes(firsts.tolist(), offs.tolist(),
                                                                          sizes_bytes.tolist()),
                           sizes_bytes, lo, b"".join(payloads), dist, rank)

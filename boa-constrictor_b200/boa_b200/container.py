@@ -167,3 +167,112 @@ def parse(data: bytes) -> Parsed:
         if lengths[i] % 4:
             raise ValueError(f"Chunk {i} length is not a whole number of u32 words")
     return Parsed(flags, ulen, chunk_len, n, last_chunk_len, fp, p, idx_pos, first_bytes, offsets, lengths)
+
+
+# ---------------------------------------------------------------------------
+# Streaming / resumable writer
+# ---------------------------------------------------------------------------
+PROVISIONAL = b"IDXP"
+
+
+def provisional_index(first_bytes, lengths) -> bytes:
+    """'IDXP' | u32 k | k x u8 first_bytes | k x uvarint(byte lengths) | u32 crc32.
+    Offsets are the running sum of the lengths (payload written in order)."""
+    idx = bytearray(PROVISIONAL) + struct.pack("<I", len(lengths))
+    idx += bytes(int(b) & 0xFF for b in first_bytes)
+    for ln in lengths:
+        idx += uvarint_encode(int(ln))
+    return bytes(idx) + struct.pack("<I", zlib.crc32(idx) & 0xFFFFFFFF)
+
+
+def parse_provisional(data: bytes, payload_start: int):
+    """(first_bytes, lengths) recorded by the last complete provisional index."""
+    pos = data.rfind(PROVISIONAL)
+    if pos < payload_start or pos + 12 > len(data):
+        raise ValueError("no provisional index: nothing to resume")
+    k, = struct.unpack_from("<I", data, pos + 4)
+    q = pos + 8
+    if q + k > len(data):
+        raise ValueError("truncated provisional index")
+    firsts = list(data[q:q + k])
+    q += k
+    lengths = []
+    mm = memoryview(data)
+    for _ in range(k):
+        ln, q = uvarint_decode(mm, q)
+        lengths.append(ln)
+    if q + 4 > len(data):
+        raise ValueError("truncated provisional index")
+    crc, = struct.unpack_from("<I", data, q)
+    if (zlib.crc32(data[pos:q]) & 0xFFFFFFFF) != crc:
+        raise ValueError("bad provisional index CRC")
+    if payload_start + sum(lengths) != pos:
+        raise ValueError("provisional index does not follow its payload")
+    return firsts, lengths
+
+
+class StreamingWriter:
+    """Write a BOA2 file wave by wave (boa.py:195-262 streams the payload the
+    same way).  After every wave the payload is followed by a provisional
+    index that records the chunks written so far, so a run that stops between
+    waves can resume after the last complete one (``resume=True``); finish()
+    replaces it with the final 'IDX1' index, which is all a reader sees."""
+
+    def __init__(self, path, header: bytes, n_chunks: int, resume: bool = False):
+        import os
+        self.path = str(path)
+        self.n_chunks = int(n_chunks)
+        self.payload_start = len(header)
+        self.firsts: list[int] = []
+        self.lengths: list[int] = []
+        if resume and os.path.exists(self.path):
+            with open(self.path, "rb") as f:
+                data = f.read()
+            if data[:len(header)] != header:
+                raise ValueError("cannot resume: the file header differs (another input, chunking or model)")
+            self.firsts, self.lengths = parse_provisional(data, self.payload_start)
+            if len(self.lengths) > self.n_chunks:
+                raise ValueError("cannot resume: the file records more chunks than the input has")
+            self.f = open(self.path, "r+b")
+        else:
+            self.f = open(self.path, "wb")
+            self.f.write(header)
+            self._write_tail(provisional_index([], []))
+
+    @property
+    def chunks_done(self) -> int:
+        return len(self.lengths)
+
+    def _end(self) -> int:
+        return self.payload_start + sum(self.lengths)
+
+    def _write_tail(self, tail: bytes):
+        self.f.seek(self._end())
+        self.f.write(tail)
+        self.f.truncate()
+        self.f.flush()
+
+    def append(self, first_bytes, payloads) -> None:
+        """Add the next chunks: their first bytes and u32 word payloads (bytes)."""
+        if self.chunks_done + len(payloads) > self.n_chunks:
+            raise ValueError("more chunks than the header declares")
+        self.f.seek(self._end())
+        for b in payloads:
+            self.f.write(b)
+        self.firsts.extend(int(x) & 0xFF for x in first_bytes)
+        self.lengths.extend(len(b) for b in payloads)
+        self._write_tail(provisional_index(self.firsts, self.lengths))
+
+    def finish(self) -> None:
+        if self.chunks_done != self.n_chunks:
+            raise ValueError(f"finish after {self.chunks_done} of {self.n_chunks} chunks")
+        offsets, off = [], 0
+        for ln in self.lengths:
+            offsets.append(off)
+            off += ln
+        self._write_tail(index_bytes(self.firsts, offsets, self.lengths))
+        self.f.close()
+
+    def close(self) -> None:
+        if not self.f.closed:
+            self.f.close()

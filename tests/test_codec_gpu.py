@@ -149,3 +149,34 @@ def test_time_blocked_encode_matches_one_position_steps(d, fmt):
     assert all(np.array_equal(a, b) for a, b in zip(comp1, comp4))
     outs = codec.decompress_GPU(m, comp4, Ls4, first4)
     assert all(np.array_equal(x.numpy(), o) for x, o in zip(xs, outs))
+
+
+def test_boafile_resume_after_interrupted_compress(tmp_path, monkeypatch):
+    """BoaFile.compress appends each wave as it is coded; a run that stops
+    after two waves resumes with resume=True and ends with the same file as an
+    uninterrupted run."""
+    from boa import BOA
+    from boa_b200 import synthetic
+    monkeypatch.setenv("BOA_GPU_STREAMS", "5")
+    data = synthetic.config_data(1)[:24000]
+    src = tmp_path / "in.bin"
+    src.write_bytes(data)
+    m = _model()
+    one = tmp_path / "one.boa"
+    BOA("cuda", str(one), m).compress(str(src), chunks_count=23, progress=False)
+    two = tmp_path / "two.boa"
+    bf = BOA("cuda", str(two), m)
+    calls = {"n": 0}
+    real = bf._encode_wave
+
+    def flaky(*a, **k):
+        calls["n"] += 1
+        if calls["n"] > 2:
+            raise KeyboardInterrupt("simulated stop")
+        return real(*a, **k)
+    bf._encode_wave = flaky
+    with pytest.raises(KeyboardInterrupt):
+        bf.compress(str(src), chunks_count=23, progress=False)
+    BOA("cuda", str(two), m).compress(str(src), chunks_count=23, progress=False, resume=True)
+    assert two.read_bytes() == one.read_bytes()
+    assert BOA("cuda", str(two), m).decompress(progress=False) == data
