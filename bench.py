@@ -170,10 +170,15 @@ def measured_peak():
         return 6650.0, "fallback 6.65 TB/s"
 
 
-def traffic_per_coded_byte():
+def traffic_per_coded_byte(d, L):
+    """ncu DRAM bytes per coded byte of the one-position kernel, for the model
+    shape the capture was taken on (None for other shapes)."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     try:
-        return float(json.load(open(p))["k_boa_step"]["dram_bytes_per_coded_byte"])
+        rec = json.load(open(p))["k_boa_step"]
+        if rec.get("model", {}) != {"d_model": d, "num_layers": L}:
+            return None
+        return float(rec["dram_bytes_per_coded_byte"])
     except Exception:
         return None
 
@@ -334,7 +339,7 @@ def run_ours(args, cfg, rank, world, local_rank, dist):
     coded = sum(max(x - 1, 0) for x in lens)
     sb = state_bytes_per_coded_byte(cfg["d"], cfg["L"])
     peak, peak_src = measured_peak()
-    tpb = traffic_per_coded_byte()
+    tpb = traffic_per_coded_byte(cfg["d"], cfg["L"])
     # dominant kernel: the decode launch (one position per kernel step)
     alg_d = sb * coded + nbytes + comp_bits // 8
     ach_d = alg_d / (t_d / args.steps) / 1e9

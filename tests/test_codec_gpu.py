@@ -180,3 +180,15 @@ def test_boafile_resume_after_interrupted_compress(tmp_path, monkeypatch):
     BOA("cuda", str(two), m).compress(str(src), chunks_count=23, progress=False, resume=True)
     assert two.read_bytes() == one.read_bytes()
     assert BOA("cuda", str(two), m).decompress(progress=False) == data
+
+
+def test_roundtrip_d512_bf16():
+    """Config-4 model shape (d_model 512, bf16 operands), fewer layers: encode
+    in time blocks, decode one position per step, lossless."""
+    import codec
+    m = _model(512, 2, "bf16")
+    lens = [1, 9, 70, 131, 40] * 3
+    xs = _chunks(13, lens)
+    comp, first, Ls = codec.compress_GPU(m, xs)
+    outs = codec.decompress_GPU(m, comp, Ls, first)
+    assert all(np.array_equal(x.numpy(), o) for x, o in zip(xs, outs))
