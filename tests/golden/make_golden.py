@@ -1,6 +1,6 @@
 """Regenerate the committed CPU golden fixtures in tests/golden/.
 
-Run in a container that has the reference tree (default /root/reference):
+Run in a container that has the reference tree (--reference points at it):
     python tests/golden/make_golden.py [--reference /path/to/reference]
 
 Fixtures:
