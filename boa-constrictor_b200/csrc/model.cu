@@ -660,7 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
               float4 stv[8 / TB];
 #pragma unroll
               for (int j = 0; j < 8; j += TB)
-                stv[j / TB] = ((lmask >> (nb + j)) & 1u) ? cs[((nb + j) / TB) * cst] : make_float4(0.f, 0.f, 0.f, 0.f);
+                stv[j / TB] = ((lmask >> (nb + j)) & 1u) ? __ldcs(&cs[((nb + j) / TB) * cst]) : make_float4(0.f, 0.f, 0.f, 0.f);
               float xv[8];
               const uint32_t col = (uint32_t)(COL_X + lt * CT + nb);
               tc::tmem_ld8(tq + col, xv);
@@ -676,7 +676,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
                 acc = fmaf(w.w, xv[j], acc);
                 const float xc = silu_fast(acc);
                 win = make_float4(win.y, win.z, xv[j], 0.f);
-                if ((smask >> n) & 1u) cs[(n / TB) * cst] = win;
+                if ((smask >> n) & 1u) __stcs(&cs[(n / TB) * cst], win);
                 put_b(buf, n, e, xc);
                 xv[j] = xc;
               }
@@ -730,13 +730,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
             const float Dp = __ldg(lp + LP::Dp + e);
             const float bdt = __ldg(lp + LP::dtb + e);
             // SSM state layout [chunk][layer][k = 0..3][channel] of float4: a
-            // warp's access for one k is 512 contiguous bytes
+            // warp's access for one k is 512 contiguous bytes.  The state is
+            // read and written once per step and far larger than L2: loads and
+            // stores carry the streaming cache hint (.cs) so they do not evict
+            // the weight tiles.
             float4* ss = a.ssm_state + ((long long)c0 * L + l) * 4 * E + e;   // chunk stride 4*L*E
             const long long cstride = (long long)L * 4 * E;
             float4 nx[4];                                   // state of the next chunk, loaded one chunk ahead
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              nx[k] = ((lmask >> n0) & 1u) ? ss[(n0 / TB) * cstride + k * E] : make_float4(0.f, 0.f, 0.f, 0.f);
+              nx[k] = ((lmask >> n0) & 1u) ? __ldcs(&ss[(n0 / TB) * cstride + k * E]) : make_float4(0.f, 0.f, 0.f, 0.f);
             float h[16];
 #pragma unroll 1
             for (int gi = 0; gi < RUN / 4; ++gi) {
@@ -756,7 +759,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
                   if (n + TB < n0 + RUN) {
 #pragma unroll
                     for (int k = 0; k < 4; ++k)
-                      nx[k] = ((lmask >> (n + TB)) & 1u) ? ss[((n + TB) / TB) * cstride + k * E]
+                      nx[k] = ((lmask >> (n + TB)) & 1u) ? __ldcs(&ss[((n + TB) / TB) * cstride + k * E])
                                                          : make_float4(0.f, 0.f, 0.f, 0.f);
                   }
                 }
@@ -783,7 +786,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
                 if ((smask >> n) & 1u) {
 #pragma unroll
                   for (int k = 0; k < 4; ++k)
-                    ss[(n / TB) * cstride + k * E] = make_float4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
+                    __stcs(&ss[(n / TB) * cstride + k * E], make_float4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]));
                 }
                 y = fmaf(Dp, xc[j], y);
                 y *= silu_fast(z[j]);
