@@ -168,7 +168,8 @@ struct Smem {
   static constexpr int o_lens = o_prev + CT * 4;
   static constexpr int o_bars = o_lens + CT * 4;
   static constexpr int kMaxStages = 12;
-  static constexpr int o_misc = o_bars + (2 * kMaxStages + 4) * 8;
+  static constexpr int kTileBars = 16;                      // per-M-tile completion barriers
+  static constexpr int o_misc = o_bars + (2 * kMaxStages + 4 + kTileBars) * 8;
   static constexpr int o_prof = o_misc + 64;                 // PF_SLOTS x u64 phase accumulators
   static constexpr int o_ring = ((o_prof + 256 + 1023) / 1024) * 1024;
   static constexpr int kBudget = 227 * 1024 - 1024;          // minus alignment slack
@@ -285,6 +286,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   constexpr int RUN = CT / RUNS;
   static_assert(RUN % 4 == 0 && RUN >= 4, "chunk run");
   static_assert(RUN % TB == 0, "a chunk run holds whole time blocks");
+  // Tile pipelining (conv / GELU start on finished in_proj / ff.0 M tiles)
+  // needs the next operand in the other buffer: only with two buffers.
+  constexpr bool kTilePipe = S::NBUF == 2;
   // column masks: first / last position of each chunk's time block
   constexpr uint32_t kColAll = CT == 32 ? 0xffffffffu : ((1u << CT) - 1u);
   constexpr uint32_t kFirstCols = [] {
@@ -308,6 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   uint64_t* act_bar = mma_bar + 1;
   uint64_t* drain_bar = act_bar + 1;
   uint64_t* xch_bar = drain_bar + 1;                      // peer finished writing an exchange
+  uint64_t* tile_bar = xch_bar + 1;                       // in_proj / ff.0: M tile t (and all before it) done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::o_misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::o_misc + 4);
   int* nsteps_sh = reinterpret_cast<int*>(smem + S::o_misc + 8);
@@ -336,6 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
     tc::mbar_init(act_bar, kComputeWarps * SPLIT);        // both CTAs' compute warps (lane 0 of each)
     tc::mbar_init(drain_bar, 1);
     tc::mbar_init(xch_bar, kComputeWarps);                // the peer's compute warps
+    for (int t = 0; t < S::kTileBars; ++t) tc::mbar_init(&tile_bar[t], 1);
     *abort_flag = 0;
     *cons_sh = 0;
     *prod_it_sh = 0;
@@ -438,7 +444,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       unsigned long long w_full = 0, w_act = 0;
       const long long t_mma0 = clock64();
       // D[col0 + mt*CT ...] = sum over ks of A(mt, ks) * B(ks)^T
-      auto gemm = [&](int n_mt, int n_ks, int col0) -> bool {
+      // tiles: also commit after every M tile, so the epilogue of a finished
+      // tile can start while later tiles run (in_proj -> conv, ff.0 -> GELU)
+      auto gemm = [&](int n_mt, int n_ks, int col0, bool tiles) -> bool {
         const uint64_t bdesc0 = bdesc_base + (uint64_t)(gemm_no % S::NBUF) * kBufDesc;
         uint32_t dcol = tmem + (uint32_t)col0;
         for (int mt = 0; mt < n_mt; ++mt, dcol += CT) {
@@ -457,10 +465,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
             *cons_sh = (int)(++it);
             if (++st == kStagesK) { st = 0; ph ^= 1u; }
           }
+          if (tiles) tc::mma_commit(&tile_bar[mt]);
         }
         return true;
       };
-      auto step_gemm = [&](int n_mt, int n_ks, int col0) -> bool {
+      auto step_gemm = [&](int n_mt, int n_ks, int col0, bool tiles = false) -> bool {
         const long long tw = prof ? clock64() : 0;
         const bool got = SPLIT == 2 ? mbar_wait_cluster(act_bar, act_phase, abort_flag, kWaitBudget)
                                     : tc::mbar_wait(act_bar, act_phase, abort_flag, kWaitBudget);
@@ -468,18 +477,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         if (prof) w_act += clock64() - tw;
         act_phase ^= 1u;
         tc::tc_fence_after();
-        if (!gemm(n_mt, n_ks, col0)) return false;
+        if (!gemm(n_mt, n_ks, col0, tiles)) return false;
         tc::mma_commit(mma_bar);
         ++gemm_no;
         return true;
       };
       for (int s = 0; s < nsteps && ok; ++s) {
         for (int l = 0; l < L && ok; ++l) {
-          ok = step_gemm(2 * LT_E, kD, 0)          // in_proj -> x | z (own channels)
+          ok = step_gemm(2 * LT_E, kD, 0, kTilePipe)    // in_proj -> x | z (own channels)
                && step_gemm(1, kE, COL_XP)         // x_proj (whole)
                && step_gemm(LT_E, 1, COL_DT)       // dt_proj (own channels)
                && step_gemm(LT_D, kE, 0)           // out_proj (own features)
-               && step_gemm(LT_F, kD, 0)           // ff.0
+               && step_gemm(LT_F, kD, 0, kTilePipe)     // ff.0
                && step_gemm(LT_D, kF, 0);          // ff.2
         }
         ok = ok && step_gemm(LT_D, kD, 0)          // head.0
@@ -577,6 +586,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       tc::tc_fence_after();
       return *abort_flag == 0;
     };
+    // Per-M-tile completion of in_proj / ff.0: a unit waits for the tile it
+    // reads; gemm_done() then waits (usually without spinning) for the whole
+    // GEMM, which keeps every barrier's phase parity in step.
+    uint32_t tile_ph = 0;
+    static_assert(2 * LT_E <= S::kTileBars && LT_F <= S::kTileBars, "tile barriers");
+    auto wait_tile = [&](int mt) {
+      if constexpr (kTilePipe) {
+        tc::mbar_wait(&tile_bar[mt], (tile_ph >> mt) & 1u, abort_flag, kWaitBudget);
+        tc::tc_fence_after();
+      }
+    };
+    auto gemm_done = [&](int n_mt) {
+      if constexpr (kTilePipe) {
+        tc::mbar_wait(mma_bar, mma_phase, abort_flag, kWaitBudget);
+        mma_phase ^= 1u;
+        tile_ph ^= (1u << n_mt) - 1u;
+        tc::tc_fence_after();
+      }
+    };
     // After writing shared values into the peer: tell it, then wait for its
     // values to have arrived here.  Uniform verdict as wait_mma.
     auto exchange = [&]() -> bool {
@@ -642,7 +670,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         layernorm_to_b(hres, lp + LP::ln1w, lp + LP::ln1b);
         arrive_act();
         mark(PF_LN1);
-        if (!(ok = wait_mma())) break;
+        if constexpr (!kTilePipe) {
+          if (!(ok = wait_mma())) break;
+        }
         mark(PF_W_IN);
         // ---- causal conv (width 4) + SiLU, thread per own channel; xc -> both
         //      CTAs' operand (x_proj runs whole) and into TMEM for the scan
@@ -650,6 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
           uint8_t* buf = bnext();
           for (int u = g; u < LT_E * NG; u += 4) {
             const int lt = u / NG;
+            wait_tile(lt);                                // x tile lt of in_proj
             const int e = (int)(rank * LT_E + lt) * 128 + row;
             const float4 w = __ldg(reinterpret_cast<const float4*>(lp + LP::convw) + e);
             const float cb = __ldg(lp + LP::convb + e);
@@ -684,6 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
             }
           }
           tc::tmem_wait_st();
+          gemm_done(2 * LT_E);                              // z tiles too, before the next GEMM's wait
           push_slices(buf, (int)rank * (LT_E * 128 / PER), LT_E * 128 / PER);   // xc: x_proj runs whole
         }
         arrive_act();
@@ -816,13 +848,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         layernorm_to_b(scr, lp + LP::ln2w, lp + LP::ln2b);
         arrive_act();
         mark(PF_LN2);
-        if (!(ok = wait_mma())) break;
+        if constexpr (!kTilePipe) {
+          if (!(ok = wait_mma())) break;
+        }
         mark(PF_W_FF1);
         // ---- ff.0 epilogue (own features): + b1, exact GELU -> both operands
         {
           uint8_t* buf = bnext();
           for (int u = g; u < LT_F * NG; u += 4) {
             const int lt = u / NG, gi = u % NG;
+            wait_tile(lt);                                // ff.0 tile lt
             const int f = (int)(rank * LT_F + lt) * 128 + row;
             const float b = __ldg(lp + LP::b1 + f);
             float v[8];
@@ -830,6 +865,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
 #pragma unroll
             for (int j = 0; j < 8; ++j) put_b(buf, 8 * gi + j, f, gelu_f(v[j] + b));
           }
+          gemm_done(LT_F);
           push_slices(buf, (int)rank * (LT_F * 128 / PER), LT_F * 128 / PER);
         }
         arrive_act();
