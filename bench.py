@@ -170,12 +170,13 @@ def measured_peak():
         return 6650.0, "fallback 6.65 TB/s"
 
 
-def traffic_per_coded_byte(d, L):
-    """ncu DRAM bytes per coded byte of the one-position kernel, for the model
-    shape the capture was taken on (None for other shapes)."""
+def traffic_per_coded_byte(d, L, key="k_boa_step"):
+    """ncu DRAM bytes per coded byte of a kernel (k_boa_step: one position per
+    step; k_boa_step_tb4: time blocks of 4), for the model shape the capture
+    was taken on (None for other shapes)."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     try:
-        rec = json.load(open(p))["k_boa_step"]
+        rec = json.load(open(p))[key]
         if rec.get("model", {}) != {"d_model": d, "num_layers": L}:
             return None
         return float(rec["dram_bytes_per_coded_byte"])
@@ -352,8 +353,10 @@ def run_ours(args, cfg, rank, world, local_rank, dist):
     tb = 4
     alg_c = sb * coded // tb + nbytes + comp_bits // 8
     ach_c = alg_c / (t_c / args.steps) / 1e9
+    tpb_c = traffic_per_coded_byte(cfg["d"], cfg["L"], "k_boa_step_tb4")
     roof_c = {"bound": "hbm", "kernel": "k_boa_step encode launch (time blocks of 4 positions)",
               "achieved": ach_c, "peak": peak, "unit": "GB/s", "frac": ach_c / peak,
+              "traffic": (tpb_c * coded if tpb_c else None),
               "algorithmic_bytes_per_launch": alg_c,
               "per_unit": f"{sb // tb} B recurrent-state read+write per coded byte"}
     cpu = None
