@@ -117,10 +117,25 @@ __device__ __forceinline__ void rc_dec_reset(RcDec& d, const uint32_t* in, int n
 }
 
 // The decode target: (point - lower) / scale, clamped to 2^P - 1.
+// floor(n / d) through a correctly rounded fp64 division and one integer
+// correction step, for operands where the fp64 quotient is within one of the
+// true floor (see the caller): exactly the integer quotient, at a fraction of
+// the cost of the 64-bit by 64-bit integer division routine.
+__device__ __forceinline__ unsigned long long udiv_f64(unsigned long long n, unsigned long long d) {
+  unsigned long long q = (unsigned long long)(__ddiv_rn((double)n, (double)d));
+  const unsigned long long p = q * d;
+  if (p > n) --q;
+  else if (n - p >= d) ++q;
+  return q;
+}
+
 __device__ __forceinline__ uint32_t rc_dec_target(const RcDec& d, int precision,
                                                   unsigned long long& scale) {
   scale = d.range >> precision;
-  unsigned long long q = (d.point - d.lower) / scale;
+  const unsigned long long num = d.point - d.lower;
+  // num < range < 2^64; with precision <= 16 the scale is >= 2^16, so the fp64
+  // rounding of num (<= 2^11) moves the quotient by less than one
+  unsigned long long q = precision <= 16 && num < (1ull << 63) ? udiv_f64(num, scale) : num / scale;
   const unsigned long long top = (1ull << precision) - 1ull;
   if (q > top) q = top;
   return (uint32_t)q;
