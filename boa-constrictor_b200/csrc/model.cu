@@ -13,9 +13,12 @@
 //   logits = W_h2 ReLU(W_h1 h + b_h1) + b_h2                    model.py:90-95
 //   then quantiser + range coder (codec.py:63-76 / 131-141).
 //
-// Design (B200-first, not a port): one persistent CTA owns CT chunks and runs
-// every timestep of every layer for them; CTAs never talk to each other
-// because the whole step is row-local per chunk.  Roles inside the CTA:
+// Design (B200-first, not a port): one persistent CTA (or a 2-CTA cluster
+// splitting the output features) owns CT operand columns and runs every
+// timestep of every layer for them; clusters never talk to each other because
+// the whole step is row-local per chunk.  A column is one chunk, or, in the
+// time-blocked encode / logits form (TB = 4), one of TB consecutive positions
+// of a chunk.  Roles inside the CTA:
 //   warp 0      streams every projection weight tile (pre-packed 16 KB SW128
 //               images, in consumption order) through a shared-memory ring
 //               with bulk async copies;
@@ -26,7 +29,7 @@
 //               epilogues straight out of TMEM, write the next B operand into
 //               shared memory, and run quantiser + range coder (a warp per chunk).
 // The recurrent state (conv window + SSM state, fp32) streams from HBM once
-// per layer per byte; everything else stays on chip.  Every accumulator column
+// per layer per kernel step (per TB bytes); everything else stays on chip.  Every accumulator column
 // depends only on its own chunk and the weights, in a fixed K order, so the
 // probabilities do not depend on batch composition, grid size or GPU.
 #include <cuda_runtime.h>
