@@ -289,9 +289,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   constexpr int RUN = CT / RUNS;
   static_assert(RUN % 4 == 0 && RUN >= 4, "chunk run");
   static_assert(RUN % TB == 0, "a chunk run holds whole time blocks");
-  // Tile pipelining (conv / GELU start on finished in_proj / ff.0 M tiles)
-  // needs the next operand in the other buffer: only with two buffers.
-  constexpr bool kTilePipe = S::NBUF == 2;
+  // Tile pipelining: the conv starts on finished in_proj M tiles, the GELU on
+  // finished ff.0 tiles, so the epilogue's writes of the next operand must not
+  // touch the operand the remaining tiles still read.  With two buffers the
+  // next operand goes to the other one.  With one buffer the x_proj operand
+  // (K = E) is placed after in_proj's (K = D) -- (D + E) <= F slices fit the
+  // buffer -- while the ff.2 operand (K = F) needs the whole buffer, so ff.0
+  // keeps the whole-GEMM wait there.
+  constexpr bool kPipeFF = S::NBUF == 2;
+  constexpr int kXOff = S::NBUF == 1 ? kD : 0;           // x_proj operand offset, K slices
   // column masks: first / last position of each chunk's time block
   constexpr uint32_t kColAll = CT == 32 ? 0xffffffffu : ((1u << CT) - 1u);
   constexpr uint32_t kFirstCols = [] {
@@ -449,8 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       // D[col0 + mt*CT ...] = sum over ks of A(mt, ks) * B(ks)^T
       // tiles: also commit after every M tile, so the epilogue of a finished
       // tile can start while later tiles run (in_proj -> conv, ff.0 -> GELU)
-      auto gemm = [&](int n_mt, int n_ks, int col0, bool tiles) -> bool {
-        const uint64_t bdesc0 = bdesc_base + (uint64_t)(gemm_no % S::NBUF) * kBufDesc;
+      auto gemm = [&](int n_mt, int n_ks, int col0, bool tiles, int b_off) -> bool {
+        const uint64_t bdesc0 = bdesc_base + (uint64_t)(gemm_no % S::NBUF) * kBufDesc + (uint64_t)b_off * kSliceDesc;
         uint32_t dcol = tmem + (uint32_t)col0;
         for (int mt = 0; mt < n_mt; ++mt, dcol += CT) {
           uint64_t bd = bdesc0;
@@ -472,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         }
         return true;
       };
-      auto step_gemm = [&](int n_mt, int n_ks, int col0, bool tiles = false) -> bool {
+      auto step_gemm = [&](int n_mt, int n_ks, int col0, bool tiles = false, int b_off = 0) -> bool {
         const long long tw = prof ? clock64() : 0;
         const bool got = SPLIT == 2 ? mbar_wait_cluster(act_bar, act_phase, abort_flag, kWaitBudget)
                                     : tc::mbar_wait(act_bar, act_phase, abort_flag, kWaitBudget);
@@ -480,18 +486,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         if (prof) w_act += clock64() - tw;
         act_phase ^= 1u;
         tc::tc_fence_after();
-        if (!gemm(n_mt, n_ks, col0, tiles)) return false;
+        if (!gemm(n_mt, n_ks, col0, tiles, b_off)) return false;
         tc::mma_commit(mma_bar);
         ++gemm_no;
         return true;
       };
       for (int s = 0; s < nsteps && ok; ++s) {
         for (int l = 0; l < L && ok; ++l) {
-          ok = step_gemm(2 * LT_E, kD, 0, kTilePipe)    // in_proj -> x | z (own channels)
-               && step_gemm(1, kE, COL_XP)         // x_proj (whole)
+          ok = step_gemm(2 * LT_E, kD, 0, true)    // in_proj -> x | z (own channels)
+               && step_gemm(1, kE, COL_XP, false, kXOff)   // x_proj (whole)
                && step_gemm(LT_E, 1, COL_DT)       // dt_proj (own channels)
                && step_gemm(LT_D, kE, 0)           // out_proj (own features)
-               && step_gemm(LT_F, kD, 0, kTilePipe)     // ff.0
+               && step_gemm(LT_F, kD, 0, kPipeFF)  // ff.0
                && step_gemm(LT_D, kF, 0);          // ff.2
         }
         ok = ok && step_gemm(LT_D, kD, 0)          // head.0
@@ -595,18 +601,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
     uint32_t tile_ph = 0;
     static_assert(2 * LT_E <= S::kTileBars && LT_F <= S::kTileBars, "tile barriers");
     auto wait_tile = [&](int mt) {
-      if constexpr (kTilePipe) {
-        tc::mbar_wait(&tile_bar[mt], (tile_ph >> mt) & 1u, abort_flag, kWaitBudget);
-        tc::tc_fence_after();
-      }
+      tc::mbar_wait(&tile_bar[mt], (tile_ph >> mt) & 1u, abort_flag, kWaitBudget);
+      tc::tc_fence_after();
     };
     auto gemm_done = [&](int n_mt) {
-      if constexpr (kTilePipe) {
-        tc::mbar_wait(mma_bar, mma_phase, abort_flag, kWaitBudget);
-        mma_phase ^= 1u;
-        tile_ph ^= (1u << n_mt) - 1u;
-        tc::tc_fence_after();
-      }
+      tc::mbar_wait(mma_bar, mma_phase, abort_flag, kWaitBudget);
+      mma_phase ^= 1u;
+      tile_ph ^= (1u << n_mt) - 1u;
+      tc::tc_fence_after();
     };
     // After writing shared values into the peer: tell it, then wait for its
     // values to have arrived here.  Uniform verdict as wait_mma.
@@ -673,14 +675,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         layernorm_to_b(hres, lp + LP::ln1w, lp + LP::ln1b);
         arrive_act();
         mark(PF_LN1);
-        if constexpr (!kTilePipe) {
-          if (!(ok = wait_mma())) break;
-        }
         mark(PF_W_IN);
         // ---- causal conv (width 4) + SiLU, thread per own channel; xc -> both
         //      CTAs' operand (x_proj runs whole) and into TMEM for the scan
         {
-          uint8_t* buf = bnext();
+          uint8_t* buf = bnext() + kXOff * CT * 128;      // x_proj operand (after in_proj's with one buffer)
           for (int u = g; u < LT_E * NG; u += 4) {
             const int lt = u / NG;
             wait_tile(lt);                                // x tile lt of in_proj
@@ -851,7 +850,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         layernorm_to_b(scr, lp + LP::ln2w, lp + LP::ln2b);
         arrive_act();
         mark(PF_LN2);
-        if constexpr (!kTilePipe) {
+        if constexpr (!kPipeFF) {
           if (!(ok = wait_mma())) break;
         }
         mark(PF_W_FF1);
@@ -860,7 +859,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
           uint8_t* buf = bnext();
           for (int u = g; u < LT_F * NG; u += 4) {
             const int lt = u / NG, gi = u % NG;
-            wait_tile(lt);                                // ff.0 tile lt
+            if constexpr (kPipeFF) wait_tile(lt);         // ff.0 tile lt
             const int f = (int)(rank * LT_F + lt) * 128 + row;
             const float b = __ldg(lp + LP::b1 + f);
             float v[8];
@@ -868,7 +867,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
 #pragma unroll
             for (int j = 0; j < 8; ++j) put_b(buf, 8 * gi + j, f, gelu_f(v[j] + b));
           }
-          gemm_done(LT_F);
+          if constexpr (kPipeFF) gemm_done(LT_F);
           push_slices(buf, (int)rank * (LT_F * 128 / PER), LT_F * 128 / PER);
         }
         arrive_act();
