@@ -294,10 +294,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   // touch the operand the remaining tiles still read.  With two buffers the
   // next operand goes to the other one.  With one buffer the x_proj operand
   // (K = E) is placed after in_proj's (K = D) -- (D + E) <= F slices fit the
-  // buffer -- while the ff.2 operand (K = F) needs the whole buffer, so ff.0
-  // keeps the whole-GEMM wait there.
-  constexpr bool kPipeFF = S::NBUF == 2;
+  // buffer -- and the GELU tiles that would overwrite ff.0's operand wait for
+  // the whole GEMM.
   constexpr int kXOff = S::NBUF == 1 ? kD : 0;           // x_proj operand offset, K slices
+  // first ff.0 M tile whose GELU output (K slices [t*128/PER, (t+1)*128/PER)
+  // of the ff.2 operand) misses ff.0's operand (slices [0, kD)) in one buffer
+  constexpr int kSafeTile = S::NBUF == 2 ? 0 : (D + 127) / 128;
   // column masks: first / last position of each chunk's time block
   constexpr uint32_t kColAll = CT == 32 ? 0xffffffffu : ((1u << CT) - 1u);
   constexpr uint32_t kFirstCols = [] {
@@ -497,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
                && step_gemm(1, kE, COL_XP, false, kXOff)   // x_proj (whole)
                && step_gemm(LT_E, 1, COL_DT)       // dt_proj (own channels)
                && step_gemm(LT_D, kE, 0)           // out_proj (own features)
-               && step_gemm(LT_F, kD, 0, kPipeFF)  // ff.0
+               && step_gemm(LT_F, kD, 0, true)     // ff.0
                && step_gemm(LT_D, kF, 0);          // ff.2
         }
         ok = ok && step_gemm(LT_D, kD, 0)          // head.0
@@ -850,24 +852,37 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         layernorm_to_b(scr, lp + LP::ln2w, lp + LP::ln2b);
         arrive_act();
         mark(PF_LN2);
-        if constexpr (!kPipeFF) {
-          if (!(ok = wait_mma())) break;
-        }
         mark(PF_W_FF1);
-        // ---- ff.0 epilogue (own features): + b1, exact GELU -> both operands
+        // ---- ff.0 epilogue (own features): + b1, exact GELU -> both operands.
+        //      Units start on finished ff.0 tiles.  With one buffer the GELU
+        //      output of tiles below kSafeTile would land on the K slices of
+        //      ff.0's own operand, which later tiles still read: those run
+        //      after the whole GEMM.
         {
           uint8_t* buf = bnext();
-          for (int u = g; u < LT_F * NG; u += 4) {
+          auto gelu_unit = [&](int u) {
             const int lt = u / NG, gi = u % NG;
-            if constexpr (kPipeFF) wait_tile(lt);         // ff.0 tile lt
             const int f = (int)(rank * LT_F + lt) * 128 + row;
             const float b = __ldg(lp + LP::b1 + f);
             float v[8];
             tc::tmem_ld8(tq + (uint32_t)(lt * CT + 8 * gi), v);
 #pragma unroll
             for (int j = 0; j < 8; ++j) put_b(buf, 8 * gi + j, f, gelu_f(v[j] + b));
+          };
+          if constexpr (kSafeTile == 0) {
+            for (int u = g; u < LT_F * NG; u += 4) {
+              wait_tile(u / NG);                          // ff.0 tile u / NG
+              gelu_unit(u);
+            }
+            gemm_done(LT_F);
+          } else {
+            for (int u = kSafeTile * NG + g; u < LT_F * NG; u += 4) {
+              wait_tile(u / NG);
+              gelu_unit(u);
+            }
+            gemm_done(LT_F);
+            for (int u = g; u < kSafeTile * NG; u += 4) gelu_unit(u);
           }
-          if constexpr (kPipeFF) gemm_done(LT_F);
           push_slices(buf, (int)rank * (LT_F * 128 / PER), LT_F * 128 / PER);
         }
         arrive_act();
