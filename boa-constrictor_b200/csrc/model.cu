@@ -1562,6 +1562,43 @@ BOA_API int boa_codec_decode(boa_model* m, int n_chunks, const uint32_t* d_words
   return check_err(m, s);
 }
 
+// Every wait in the kernels is bounded: when the budget runs out the waiting
+// thread raises the abort flag, the kernel winds down and the host reports
+// BOA_ERR_TIMEOUT with the context still usable.  This entry point exercises
+// that path on purpose: one thread waits on an mbarrier nothing arrives at.
+__global__ void k_diag_timeout(long long budget, uint32_t* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !tc::mbar_wait(&bar, 0, &abort_flag, budget)) atomicOr(err, RC_ERR_TIMEOUT);
+  __syncthreads();
+}
+
+BOA_API int boa_diag_timeout(int64_t budget_cycles, int device) {
+  if (budget_cycles < 1000 || budget_cycles > 20000000000LL)
+    return boa_fail(BOA_ERR_ARG, "boa_diag_timeout: budget out of range");
+  BOA_CUDA(cudaSetDevice(device));
+  uint32_t* d_e = nullptr;
+  cudaError_t e = cudaMalloc(&d_e, 4);
+  if (e == cudaSuccess) e = cudaMemset(d_e, 0, 4);
+  if (e == cudaSuccess) {
+    k_diag_timeout<<<1, 64>>>((long long)budget_cycles, d_e);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  uint32_t err = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&err, d_e, 4, cudaMemcpyDeviceToHost);
+  cudaFree(d_e);
+  if (e != cudaSuccess) return boa_fail(BOA_ERR_CUDA, std::string("boa_diag_timeout: ") + cudaGetErrorString(e));
+  if (err & RC_ERR_TIMEOUT) return boa_fail(BOA_ERR_TIMEOUT, "boa_diag_timeout: the bounded wait ran out");
+  return BOA_OK;
+}
+
 BOA_API int boa_diag_gemm(int weight_format, int M, int K, const float* h_w, const float* h_x, float* h_out,
                           int device) {
   if (weight_format < 0 || weight_format > 2) return boa_fail(BOA_ERR_ARG, "boa_diag_gemm: bad format");

@@ -190,6 +190,11 @@ BOA_API int boa_codec_decode(boa_model* m, int n_chunks, const uint32_t* d_words
 /* One CTA of the model kernel's projection pipeline on host data:
  * out[M][16] = W[M][K] . X[16][K]^T with W packed into the kernel's SW128 tiles
  * (weight_format as for boa_model_create).  Synchronous; allocates scratch. */
+/* Failure-path check (no reference counterpart): launches one thread that
+ * waits on a barrier nothing arrives at, with the same bounded wait every
+ * kernel of the library uses.  Returns BOA_ERR_TIMEOUT once budget_cycles SM
+ * cycles have passed; the CUDA context stays usable.  Synchronous. */
+BOA_API int boa_diag_timeout(int64_t budget_cycles, int device);
 BOA_API int boa_diag_gemm(int weight_format, int M, int K, const float* h_w, const float* h_x, float* h_out,
                           int device);
 
