@@ -1337,8 +1337,10 @@ int launch_step_t(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s,
   return launch_step_ct<D, KIND, 16, 1>(a, n_chunks, s);
 }
 
+#ifdef BOA_PHASE_PROFILE
 // BOA_PHASE_PROFILE=1: time the phases of CTA 0 and print them (SM cycles) to stderr.
 int launch_step_profiled(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s);
+#endif
 
 int launch_step(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
 #ifdef BOA_PHASE_PROFILE
@@ -1363,6 +1365,7 @@ int launch_step(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
   return boa_fail(BOA_ERR_UNSUPPORTED, "d_model must be 64, 256 or 512");
 }
 
+#ifdef BOA_PHASE_PROFILE
 int launch_step_profiled(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
   unsigned long long* d = nullptr;
   BOA_CUDA(cudaMalloc(&d, PF_SLOTS * sizeof(unsigned long long)));
@@ -1386,6 +1389,7 @@ int launch_step_profiled(const boa_model* m, StepArgs& a, int n_chunks, cudaStre
   a.prof = nullptr;
   return rc;
 }
+#endif
 
 int check_err(const boa_model* m, cudaStream_t s) {
   uint32_t e = 0;
