@@ -25,6 +25,8 @@
 //   warp 1      allocates TMEM and issues tcgen05.mma: weights are the A
 //               operand (M = 128 output features per tile), the chunks'
 //               activations the B operand (N = CT), accumulators in TMEM;
+//   warp 18     (single-CTA kernels) a second issuer: the M tiles of every
+//               GEMM alternate between warps 1 and 18;
 //   warps 2-17  (512 threads) run the LayerNorms, conv/scan/gate, MLP and head
 //               epilogues straight out of TMEM, write the next B operand into
 //               shared memory, and run quantiser + range coder (a warp per chunk).
@@ -42,6 +44,8 @@
 #include <cstdlib>
 #include <string>
 #include <vector>
+#include <algorithm>
+#include <utility>
 
 #include "boa_b200.h"
 #include "capi_util.h"
@@ -53,7 +57,10 @@ namespace boa {
 constexpr int kTileBytes = 16384;      // one A tile: 128 rows x 128 bytes
 constexpr int kComputeThreads = 512;   // warps 2..17
 constexpr int kComputeWarps = kComputeThreads / 32;
-constexpr int kThreads = 576;
+constexpr int kIssuer2Warp = 18;       // second MMA issuer (single-CTA kernels)
+// Threads per CTA: producer warp, MMA warp, 16 compute warps, and in the
+// single-CTA kernels a second MMA-issuing warp.
+__host__ __device__ constexpr int threads_for(int split) { return split == 1 ? 608 : 576; }
 constexpr int kCT = 16;                // chunks per CTA of the diagnostic GEMM
 constexpr long long kWaitBudget = 4000000000LL;  // SM clock cycles per bounded wait (~2 s)
 
@@ -263,7 +270,7 @@ __device__ __forceinline__ void fence_proxy_async_cluster() {
 // as in the one-position step, so the logits, and hence the bitstream, are
 // bit for bit those of the TB = 1 kernel that decode uses.
 template <int D, int KIND, int CT_, int SPLIT, int TB>
-__global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant__ StepArgs a) {
+__global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid_constant__ StepArgs a) {
   using S = Smem<D, KIND, CT_, SPLIT>;
   using LP = LayerParams<D>;
   constexpr int CT = S::CT;
@@ -272,6 +279,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   static_assert(TB == 1 || SPLIT == 1, "time blocks run on single CTAs");
   constexpr int NG = CT / 8;                             // groups of 8 chunks
   constexpr int kStagesK = S::STAGES;
+  // Issuing a tcgen05.mma costs the issuing thread about as long as the tensor
+  // core needs for it at N <= 64, so single-CTA kernels (whose GEMMs have two
+  // or more M tiles) issue from two threads.  Each issuer walks the whole tile
+  // sequence and issues the M tiles mt with mt % 2 == its index; every
+  // accumulator still sums its K slices in the same order.
+  constexpr int kIssuers = SPLIT == 1 ? 2 : 1;
+  // With two consumers of one ring an issuer skips the other's tiles and may
+  // reach a slot a whole ring round ahead of it, where the full barrier's
+  // phase parity alone would be ambiguous.  The producer therefore records,
+  // per slot, the (16-bit) index of the tile it is loading after the slot's
+  // previous tile was consumed; an issuer first waits for its tile's index in
+  // the slot, after which the parity wait is exact.
   constexpr int E = 2 * D, R = (D + 15) / 16, DBC = R + 32, F = 4 * D;
   constexpr int PER = 128 / tc::OpKind<KIND>::kElemBytes;
   constexpr int kD = D / PER, kE = E / PER, kF = F / PER;
@@ -323,12 +342,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   uint64_t* act_bar = mma_bar + 1;
   uint64_t* drain_bar = act_bar + 1;
   uint64_t* xch_bar = drain_bar + 1;                      // peer finished writing an exchange
-  uint64_t* tile_bar = xch_bar + 1;                       // in_proj / ff.0: M tile t (and all before it) done
+  uint64_t* tile_bar = xch_bar + 1;                       // in_proj / ff.0: M tile t done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::o_misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::o_misc + 4);
   int* nsteps_sh = reinterpret_cast<int*>(smem + S::o_misc + 8);
-  volatile int* cons_sh = reinterpret_cast<volatile int*>(smem + S::o_misc + 12);
   volatile long long* prod_it_sh = reinterpret_cast<volatile long long*>(smem + S::o_misc + 16);
+  volatile uint16_t* slot_tile = reinterpret_cast<volatile uint16_t*>(smem + S::o_misc + 24);   // [kMaxStages]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -348,14 +367,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   // ------------------------------- setup -------------------------------
   if (tid == 0) {
     for (int s = 0; s < kStagesK; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
-    tc::mbar_init(mma_bar, 1);
+    tc::mbar_init(mma_bar, kIssuers);                     // each issuer commits once per GEMM
     tc::mbar_init(act_bar, kComputeWarps * SPLIT);        // both CTAs' compute warps (lane 0 of each)
-    tc::mbar_init(drain_bar, 1);
+    tc::mbar_init(drain_bar, kIssuers);
     tc::mbar_init(xch_bar, kComputeWarps);                // the peer's compute warps
     for (int t = 0; t < S::kTileBars; ++t) tc::mbar_init(&tile_bar[t], 1);
     *abort_flag = 0;
-    *cons_sh = 0;
     *prod_it_sh = 0;
+    if constexpr (kIssuers == 2)
+      for (int s = 0; s < S::kMaxStages; ++s) slot_tile[s] = 0xffffu;
     int ns = 0;
     if (mode == MODE_LOGITS) {
       ns = a.n_steps;
@@ -424,6 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
           const long long tw = prof ? clock64() : 0;
           if (!tc::mbar_wait(&empty[st], ph ^ 1u, abort_flag, kWaitBudget)) { ok = false; break; }
           if (prof) w_empty += clock64() - tw;
+          if constexpr (kIssuers == 2) slot_tile[st] = (uint16_t)it;
           tc::mbar_arrive_expect_tx(&full[st], kTileBytes);
           tc::bulk_g2s(ring + st * kTileBytes, src, kTileBytes, &full[st], pol);
           if (++st == kStagesK) { st = 0; ph ^= 1u; }
@@ -432,8 +453,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       if (prof) a.prof[PF_PROD_WAIT_EMPTY] = w_empty;
       *prod_it_sh = it;   // copies issued; teardown drains the unconsumed ones on abort
     }
-  } else if (warp == 1) {
-    // ============================= MMA issuer =============================
+  } else if (warp == 1 || (kIssuers == 2 && warp == kIssuer2Warp)) {
+    // ============================= MMA issuers ============================
+    const int p = warp == 1 ? 0 : 1;
     if (lane == 0 && nsteps > 0) {
       const uint32_t id = tc::idesc<KIND>(128, CT);
       const uint64_t adesc0 = tc::sdesc_sw128(tc::smem_u32(ring));
@@ -448,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       int gemm_no = 0;                                     // selects the operand buffer
       bool ok = true;
 #ifdef BOA_PHASE_PROFILE
-      const bool prof = a.prof != nullptr && blockIdx.x == 0;
+      const bool prof = a.prof != nullptr && blockIdx.x == 0 && p == 0;
 #else
       constexpr bool prof = false;
 #endif
@@ -457,26 +479,54 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
       // D[col0 + mt*CT ...] = sum over ks of A(mt, ks) * B(ks)^T
       // tiles: also commit after every M tile, so the epilogue of a finished
       // tile can start while later tiles run (in_proj -> conv, ff.0 -> GELU)
+      // One weight tile: wait for it, issue its four K16 MMAs, release the slot.
+      auto tile_mma = [&](uint32_t dcol, uint64_t bd, bool acc) -> bool {
+        const long long tw = prof ? clock64() : 0;
+        if constexpr (kIssuers == 2) {                     // the producer has moved this slot on to tile `it`
+          const long long t0 = clock64();
+          while (slot_tile[st] != (uint16_t)it) {
+            if (*abort_flag) return false;
+            if (clock64() - t0 > kWaitBudget) { *abort_flag = 1; return false; }
+          }
+        }
+        if (!tc::mbar_wait(&full[st], ph, abort_flag, kWaitBudget)) return false;
+        if (prof) w_full += clock64() - tw;
+        tc::tc_fence_after();
+        const uint64_t ad = adesc0 + (uint64_t)st * kTileDesc;
+        tc::mma<KIND>(dcol, ad, bd, id, acc ? 1u : 0u);
+        tc::mma<KIND>(dcol, ad + 2, bd + 2, id, 1u);       // +32 bytes of K
+        tc::mma<KIND>(dcol, ad + 4, bd + 4, id, 1u);
+        tc::mma<KIND>(dcol, ad + 6, bd + 6, id, 1u);
+        tc::mma_commit(&empty[st]);
+        return true;
+      };
+      auto next_tile = [&]() {
+        ++it;
+        if (++st == kStagesK) { st = 0; ph ^= 1u; }
+      };
+      // D[col0 + mt*CT ...] = sum over ks of A(mt, ks) * B(ks)^T, K slices in order.
+      // Cluster kernels take the tiles M tile by M tile; single-CTA kernels
+      // take M tiles in pairs with their K slices interleaved (the packing
+      // order of their weight stream), tile (2q + h, ks) going to issuer h.
+      // tiles: also commit after every M tile (pair), so the epilogue of a
+      // finished tile can start while later tiles run (in_proj -> conv, ff.0 -> GELU)
       auto gemm = [&](int n_mt, int n_ks, int col0, bool tiles, int b_off) -> bool {
         const uint64_t bdesc0 = bdesc_base + (uint64_t)(gemm_no % S::NBUF) * kBufDesc + (uint64_t)b_off * kSliceDesc;
-        uint32_t dcol = tmem + (uint32_t)col0;
-        for (int mt = 0; mt < n_mt; ++mt, dcol += CT) {
+        constexpr int kGroup = SPLIT == 1 ? 2 : 1;          // M tiles whose K slices interleave
+        for (int m0 = 0; m0 < n_mt; m0 += kGroup) {
+          const int nm = n_mt - m0 < kGroup ? n_mt - m0 : kGroup;
           uint64_t bd = bdesc0;
           for (int ks = 0; ks < n_ks; ++ks, bd += kSliceDesc) {
-            const long long tw = prof ? clock64() : 0;
-            if (!tc::mbar_wait(&full[st], ph, abort_flag, kWaitBudget)) return false;
-            if (prof) w_full += clock64() - tw;
-            tc::tc_fence_after();
-            const uint64_t ad = adesc0 + (uint64_t)st * kTileDesc;
-            tc::mma<KIND>(dcol, ad, bd, id, ks > 0 ? 1u : 0u);
-            tc::mma<KIND>(dcol, ad + 2, bd + 2, id, 1u);       // +32 bytes of K
-            tc::mma<KIND>(dcol, ad + 4, bd + 4, id, 1u);
-            tc::mma<KIND>(dcol, ad + 6, bd + 6, id, 1u);
-            tc::mma_commit(&empty[st]);
-            *cons_sh = (int)(++it);
-            if (++st == kStagesK) { st = 0; ph ^= 1u; }
+            for (int h = 0; h < nm; ++h) {
+              const int mt = m0 + h;
+              if (kIssuers == 1 || (mt & 1) == p)
+                if (!tile_mma(tmem + (uint32_t)(col0 + mt * CT), bd, ks > 0)) return false;
+              next_tile();
+            }
           }
-          if (tiles) tc::mma_commit(&tile_bar[mt]);
+          if (tiles)
+            for (int h = 0; h < nm; ++h)
+              if (kIssuers == 1 || ((m0 + h) & 1) == p) tc::mma_commit(&tile_bar[m0 + h]);
         }
         return true;
       };
@@ -489,7 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         act_phase ^= 1u;
         tc::tc_fence_after();
         if (!gemm(n_mt, n_ks, col0, tiles, b_off)) return false;
-        tc::mma_commit(mma_bar);
+        tc::mma_commit(mma_bar);                            // one of the kIssuers arrivals that end the GEMM
         ++gemm_no;
         return true;
       };
@@ -512,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
         a.prof[PF_TILES] = (unsigned long long)it;
         a.prof[PF_STEPS] = (unsigned long long)nsteps;
       }
-      // every issued MMA must retire before TMEM is released
+      // every issued MMA (of both issuers) must retire before TMEM is released
       tc::mma_commit(drain_bar);
       const long long t0 = clock64();
       while (!tc::mbar_try_wait(drain_bar, 0)) {
@@ -1037,8 +1087,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_boa_step(const __grid_constant_
   __syncthreads();
   if (tid == 0 && *abort_flag) {
     atomicOr(a.err, RC_ERR_TIMEOUT);
-    // weight copies issued but never consumed must land before the CTA exits
-    for (long long j = *cons_sh; j < *prod_it_sh; ++j) {
+    // weight copies still in flight must land before the CTA exits: the
+    // last kStagesK issued copies each own their ring slot's newest phase
+    const long long last = *prod_it_sh;
+    for (long long j = last > kStagesK ? last - kStagesK : 0; j < last; ++j) {
       const int sj = (int)(j % kStagesK);
       const uint32_t pj = (uint32_t)((j / kStagesK) & 1);
       const long long t0 = clock64();
@@ -1133,15 +1185,33 @@ static uint32_t to_tf32_bits(float f) {
   return u;
 }
 
-// Append the SW128 tile images of W [M_real x K] (row-major fp32; rows >= M_real
-// and columns >= K_real are zero): M tiles mt0 .. mt0+n_mt-1, each with n_ks
-// K slices, mt outer.
-static void pack_tiles(std::vector<uint8_t>& out, const float* W, int M_real, int K_real, int ldw, int mt0, int n_mt,
-                       int n_ks, int kind) {
+// One M tile of a GEMM's weights: rows [mt*128, mt*128+128) of W [M_real x K]
+// (row-major fp32, leading dimension ldw; rows >= M_real and columns >= K_real
+// are zero).
+struct MTile {
+  const float* W;
+  int M_real, K_real, ldw, mt;
+};
+
+// Append the SW128 tile images of one GEMM's M tiles, each with n_ks K slices.
+// Order: M tile by M tile, or (pairs) the K slices of M tiles 2q and 2q+1
+// interleaved -- (2q, 0), (2q+1, 0), (2q, 1), ... -- which is the order in which
+// the two MMA issuers of a single-CTA kernel take them.
+static void pack_gemm(std::vector<uint8_t>& out, const std::vector<MTile>& tiles, int n_ks, int kind, bool pairs) {
   const int eb = kind == 0 ? 4 : 2;
   const int per = 128 / eb;
-  for (int mt = mt0; mt < mt0 + n_mt; ++mt) {
-    for (int ks = 0; ks < n_ks; ++ks) {
+  std::vector<std::pair<int, int>> order;   // (index into tiles, ks)
+  const int n_mt = (int)tiles.size();
+  for (int m0 = 0; m0 < n_mt; m0 += pairs ? 2 : 1) {
+    const int nm = pairs ? std::min(2, n_mt - m0) : 1;
+    for (int ks = 0; ks < n_ks; ++ks)
+      for (int h = 0; h < nm; ++h) order.push_back({m0 + h, ks});
+  }
+  for (const auto& o : order) {
+    const float* W = tiles[o.first].W;
+    const int M_real = tiles[o.first].M_real, K_real = tiles[o.first].K_real, ldw = tiles[o.first].ldw;
+    const int mt = tiles[o.first].mt, ks = o.second;
+    {
       const size_t base = out.size();
       out.resize(base + kTileBytes, 0);
       uint8_t* t = out.data() + base;
@@ -1167,6 +1237,11 @@ static void pack_tiles(std::vector<uint8_t>& out, const float* W, int M_real, in
       }
     }
   }
+}
+
+// M tiles mt0 .. mt0+n_mt-1 of W, appended to a GEMM's tile list.
+static void add_mtiles(std::vector<MTile>& v, const float* W, int M_real, int K_real, int ldw, int mt0, int n_mt) {
+  for (int mt = mt0; mt < mt0 + n_mt; ++mt) v.push_back(MTile{W, M_real, K_real, ldw, mt});
 }
 
 }  // namespace boa
@@ -1206,21 +1281,30 @@ struct LayerW {
   const float *w_in, *w_x, *w_dt, *w_out, *w1, *w2;
 };
 
-// Pack one rank's weight stream of a `split`-way cluster in consumption order.
+// Pack one rank's weight stream of a `split`-way cluster in consumption order
+// (single-CTA streams pair up M tiles for the two MMA issuers).
 static void pack_stream(std::vector<uint8_t>& tiles, const TilePlan& p, int rank, int D, int V, int kind,
                         const std::vector<LayerW>& lw, const float* wh0, const float* wh2) {
   const int E = 2 * D, R = cdiv(D, 16), DBC = R + 32, F = 4 * D;
+  const bool pairs = p.split == 1;
+  auto gemm = [&](const float* W, int M_real, int K_real, int ldw, int mt0, int n_mt, int n_ks) {
+    std::vector<MTile> v;
+    add_mtiles(v, W, M_real, K_real, ldw, mt0, n_mt);
+    pack_gemm(tiles, v, n_ks, kind, pairs);
+  };
   for (const LayerW& w : lw) {
-    pack_tiles(tiles, w.w_in, 2 * E, D, D, rank * p.ltE, p.ltE, p.kD, kind);            // x rows
-    pack_tiles(tiles, w.w_in, 2 * E, D, D, p.mtE + rank * p.ltE, p.ltE, p.kD, kind);    // z rows
-    pack_tiles(tiles, w.w_x, DBC, E, E, 0, 1, p.kE, kind);
-    pack_tiles(tiles, w.w_dt, E, R, R, rank * p.ltE, p.ltE, 1, kind);
-    pack_tiles(tiles, w.w_out, D, E, E, rank * p.ltD, p.ltD, p.kE, kind);
-    pack_tiles(tiles, w.w1, F, D, D, rank * p.ltF, p.ltF, p.kD, kind);
-    pack_tiles(tiles, w.w2, D, F, F, rank * p.ltD, p.ltD, p.kF, kind);
+    std::vector<MTile> in;                                                   // x rows, then z rows
+    add_mtiles(in, w.w_in, 2 * E, D, D, rank * p.ltE, p.ltE);
+    add_mtiles(in, w.w_in, 2 * E, D, D, p.mtE + rank * p.ltE, p.ltE);
+    pack_gemm(tiles, in, p.kD, kind, pairs);
+    gemm(w.w_x, DBC, E, E, 0, 1, p.kE);
+    gemm(w.w_dt, E, R, R, rank * p.ltE, p.ltE, 1);
+    gemm(w.w_out, D, E, E, rank * p.ltD, p.ltD, p.kE);
+    gemm(w.w1, F, D, D, rank * p.ltF, p.ltF, p.kD);
+    gemm(w.w2, D, F, F, rank * p.ltD, p.ltD, p.kF);
   }
-  pack_tiles(tiles, wh0, D, D, D, rank * p.ltD, p.ltD, p.kD, kind);
-  pack_tiles(tiles, wh2, V, D, D, rank * p.ltV, p.ltV, p.kD, kind);
+  gemm(wh0, D, D, D, rank * p.ltD, p.ltD, p.kD);
+  gemm(wh2, V, D, D, rank * p.ltV, p.ltV, p.kD);
 }
 
 template <int D>
@@ -1284,11 +1368,11 @@ int launch_step_ct(StepArgs& a, int n_chunks, cudaStream_t s) {
   BOA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int grid = cdiv(n_chunks, CT / TB) * SPLIT;
   if constexpr (SPLIT == 1) {
-    kern<<<grid, kThreads, smem, s>>>(a);
+    kern<<<grid, threads_for(SPLIT), smem, s>>>(a);
   } else {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(threads_for(SPLIT), 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -1611,7 +1695,11 @@ BOA_API int boa_diag_gemm(int weight_format, int M, int K, const float* h_w, con
     return boa_fail(BOA_ERR_ARG, "boa_diag_gemm: M in {128..512} step 128, K multiple of the slice, <= 1024");
   BOA_CUDA(cudaSetDevice(device));
   std::vector<uint8_t> tiles;
-  pack_tiles(tiles, h_w, M, K, K, 0, M / 128, K / per, weight_format);
+  {
+    std::vector<MTile> v;
+    add_mtiles(v, h_w, M, K, K, 0, M / 128);
+    pack_gemm(tiles, v, K / per, weight_format, false);   // M tile by M tile, as k_diag_gemm reads them
+  }
   uint8_t* d_t = nullptr; float *d_x = nullptr, *d_o = nullptr; uint32_t* d_e = nullptr;
   cudaError_t e = cudaMalloc(&d_t, tiles.size());
   if (e == cudaSuccess) e = cudaMalloc(&d_x, (size_t)kCT * K * 4);
