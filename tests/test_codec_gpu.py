@@ -87,6 +87,23 @@ def test_boafile_roundtrip_config1(tmp_path):
     assert meta["n_chunks"] == 16 and meta["uncompressed_len"] == len(data)
 
 
+def test_boafile_input_errors(tmp_path):
+    """boa.py:164 and codec.py:24-28: an empty input is a ValueError, a split
+    that leaves a chunk shorter than one byte an AssertionError; a file that is
+    not BOA2 is a ValueError on read."""
+    from boa import BOA
+    m = _model()
+    empty = tmp_path / "empty.bin"; empty.write_bytes(b"")
+    with pytest.raises(ValueError, match="empty"):
+        BOA("cuda", str(tmp_path / "e.boa"), m).compress(str(empty), progress=False)
+    one = tmp_path / "one.bin"; one.write_bytes(b"x")
+    with pytest.raises(AssertionError):
+        BOA("cuda", str(tmp_path / "o.boa"), m).compress(str(one), chunks_count=16, progress=False)
+    junk = tmp_path / "junk.boa"; junk.write_bytes(b"NOPE" + bytes(64))
+    with pytest.raises(ValueError):
+        BOA("cuda", str(junk), m).decompress(progress=False)
+
+
 def test_compressed_size_vs_oracle_ideal():
     """Code length within 0.5% of the oracle's ideal -sum log2 p (fp64 model,
     exact softmax) over the coded bytes, plus the 2-3 flush words per chunk."""

@@ -90,3 +90,5 @@ def test_reader_rejects_corruption():
         C.parse(bytes(bad))
     with pytest.raises(ValueError):
         C.parse(good[:len(good) // 2])
+    with pytest.raises(ValueError, match="Index not found"):
+        C.parse(good.replace(C.IDX, b"XXXX"))
