@@ -404,7 +404,7 @@ def coder_cpu_baseline(seconds_target=15.0):
     import numpy as np
     import torch
     from oracle import orc
-    n_thr = max(1, os.cpu_count() or 1)
+    n_thr = min(64, max(1, os.cpu_count() or 1))   # at most 64 shares (<= 270 MB of logits)
     per, t = 16, 256                     # streams per thread, symbols per stream
     n = per * n_thr
     logits, sym = _coder_slab(n, t, 4, torch.device("cpu"))
