@@ -295,6 +295,17 @@ static int rc_grid_warps(int n) {
   return blocks < cap ? (blocks < 1 ? 1 : blocks) : cap;
 }
 
+// The BQ kernels load each row of K = 256 or 1024 logits as float4 (Q % 4 == 0
+// and K == 32 * Q): those rows must start on 16-byte boundaries.  Checked on
+// the host so a misaligned pointer is an argument error, not a device fault.
+static int bq_rows_aligned(int K, const float* rows, int64_t row_stride, const char* who) {
+  if (K != 256 && K != 1024) return BOA_OK;
+  if ((reinterpret_cast<uintptr_t>(rows) & 15u) != 0 || (row_stride & 3) != 0)
+    return boa_fail(BOA_ERR_ARG, std::string(who) + ": with K = 256 or 1024 the logits rows (and the per-step "
+                                                    "stride) must be 16-byte aligned");
+  return BOA_OK;
+}
+
 extern "C" {
 
 BOA_API int boa_rc_create(boa_rc_batch** out, int n_streams, int k_symbols, int pitch_words,
@@ -411,6 +422,10 @@ BOA_API int boa_rc_device_buffers(boa_rc_batch* b, uint32_t** words, int32_t** s
 BOA_API int boa_rc_encode_step(boa_rc_batch* b, const int32_t* d_symbols, const float* d_rows,
                                const uint8_t* d_mask, void* stream) {
   if (!b || !d_symbols || !d_rows) return boa_fail(BOA_ERR_ARG, "boa_rc_encode_step: null argument");
+  if (b->quantiser == BOA_QUANT_BQ) {
+    const int rc = bq_rows_aligned(b->K, d_rows, 0, "boa_rc_encode_step");
+    if (rc) return rc;
+  }
   BOA_CUDA(cudaSetDevice(b->device));
   cudaStream_t s = (cudaStream_t)stream;
   if (b->quantiser == BOA_QUANT_BQ) {
@@ -449,6 +464,10 @@ BOA_API int boa_rc_init_decoder(boa_rc_batch* b, void* stream) {
 BOA_API int boa_rc_decode_step(boa_rc_batch* b, const float* d_rows, int32_t* d_out_symbols,
                                const uint8_t* d_mask, void* stream) {
   if (!b || !d_rows || !d_out_symbols) return boa_fail(BOA_ERR_ARG, "boa_rc_decode_step: null argument");
+  if (b->quantiser == BOA_QUANT_BQ) {
+    const int rc = bq_rows_aligned(b->K, d_rows, 0, "boa_rc_decode_step");
+    if (rc) return rc;
+  }
   BOA_CUDA(cudaSetDevice(b->device));
   cudaStream_t s = (cudaStream_t)stream;
   if (b->quantiser == BOA_QUANT_BQ) {
@@ -473,6 +492,7 @@ BOA_API int boa_rc_encode_steps(boa_rc_batch* b, int n_steps, int period, const 
   if (!b || !d_symbols || !d_rows || n_steps < 0) return boa_fail(BOA_ERR_ARG, "boa_rc_encode_steps: bad argument");
   if (b->quantiser != BOA_QUANT_BQ)
     return boa_fail(BOA_ERR_UNSUPPORTED, "boa_rc_encode_steps: BOA_QUANT_BQ handles only");
+  if (const int rc = bq_rows_aligned(b->K, d_rows, row_stride, "boa_rc_encode_steps")) return rc;
   if (n_steps == 0) return BOA_OK;
   BOA_CUDA(cudaSetDevice(b->device));
   cudaStream_t s = (cudaStream_t)stream;
@@ -495,6 +515,7 @@ BOA_API int boa_rc_decode_steps(boa_rc_batch* b, int n_steps, int period, const 
   if (!b || !d_rows || !d_out_symbols || n_steps < 0) return boa_fail(BOA_ERR_ARG, "boa_rc_decode_steps: bad argument");
   if (b->quantiser != BOA_QUANT_BQ)
     return boa_fail(BOA_ERR_UNSUPPORTED, "boa_rc_decode_steps: BOA_QUANT_BQ handles only");
+  if (const int rc = bq_rows_aligned(b->K, d_rows, row_stride, "boa_rc_decode_steps")) return rc;
   if (n_steps == 0) return BOA_OK;
   BOA_CUDA(cudaSetDevice(b->device));
   cudaStream_t s = (cudaStream_t)stream;
@@ -516,13 +537,15 @@ BOA_API int boa_rc_decode_steps(boa_rc_batch* b, int n_steps, int period, const 
 // ---------------------------------------------------------------------------
 // Allocation-free whole-stream encode.
 //
-// Some callers cannot allocate device memory when they code: a host that
-// captures its work into a CUDA graph (cudaMalloc is not allowed while a
-// stream is being captured), a plugin host or real-time service that forbids
-// allocation after start-up, or code that must not fragment a memory pool it
+// Some callers cannot allocate device memory when they code: a plugin host or
+// framework that owns the device memory pool and forbids allocation after
+// start-up, a real-time service that must not stall on cudaMalloc (which can
+// synchronise the device), or code that must not fragment a memory pool it
 // does not own.  boa_rc_encode_noalloc serves them: the caller passes the
 // inputs and the outputs, and the per-stream coder state (the scratch that
 // boa_rc_create would allocate) lives in the file-scope array below instead.
+// Each call ends by copying the array's error word back to the host, so it
+// synchronises the caller's stream.
 //
 // Limits and sharing:
 //   * at most kNoAllocMaxStreams streams per call (2 MiB of state); larger
@@ -534,7 +557,9 @@ BOA_API int boa_rc_decode_steps(boa_rc_batch* b, int n_steps, int period, const 
 //     each other's output;
 //   * every GPU that loads this library keeps the array until process exit;
 //   * the first call on a device looks up the array's device address
-//     (cudaGetSymbolAddress); make that first call before any stream capture.
+//     (cudaGetSymbolAddress) and caches it for the life of the process: a
+//     device reset (cudaDeviceReset) invalidates the cached address and is not
+//     supported while the library is loaded.
 // ---------------------------------------------------------------------------
 namespace boa {
 constexpr int kNoAllocMaxStreams = 1 << 16;
@@ -580,6 +605,8 @@ extern "C" BOA_API int boa_rc_encode_noalloc(int n_streams, int k_symbols, int n
     return boa_fail(BOA_ERR_ARG, "boa_rc_encode_noalloc: precision out of range for K");
   if (!d_words || !d_sizes || (n_steps > 0 && (!d_logits || !d_symbols)))
     return boa_fail(BOA_ERR_ARG, "boa_rc_encode_noalloc: null argument");
+  if (n_steps > 0)
+    if (const int rc = bq_rows_aligned(k_symbols, d_logits, 0, "boa_rc_encode_noalloc")) return rc;
   int device = 0;
   BOA_CUDA(cudaGetDevice(&device));
   void* base = nullptr;

@@ -146,6 +146,34 @@ __device__ __forceinline__ void tmem_ld4(uint32_t taddr, float (&v)[4]) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
 }
+// Two 8-column loads (32 lanes each) at a0 and a1, summed: the hi and lo
+// accumulators of eight value columns of a split-kind GEMM.
+__device__ __forceinline__ void tmem_ld8_sum(uint32_t a0, uint32_t a1, float (&v)[8]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%16];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%17];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(a0), "r"(a1)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]) + __uint_as_float(r[8 + i]);
+}
+__device__ __forceinline__ void tmem_ld4_sum(uint32_t a0, uint32_t a1, float (&v)[4]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%8];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%4,%5,%6,%7}, [%9];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(a0), "r"(a1)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]) + __uint_as_float(r[4 + i]);
+}
+
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
@@ -182,23 +210,42 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
   return d;
 }
 
-// Operand kinds (the BOA_WEIGHTS_* values): 0 = tf32 (fp32 storage), 1 = bf16, 2 = fp16.
+// Operand kinds (the BOA_WEIGHTS_* values): 0 = tf32 (fp32 storage), 1 = bf16,
+// 2 = fp16, 3 = 3xTF32.  kHiLo = 2 marks the split kind: every fp32 value v is
+// stored as two tf32 halves, hi = rna_tf32(v) and lo = rna_tf32(v - hi).  The
+// activation operand B carries the halves as separate rows (hi of value column
+// n in row n, lo in row n + CT/2, so one MMA with N = CT multiplies a weight
+// tile by both), and every weight tile is followed by the tile of its lo
+// halves.  An accumulator column n < CT/2 then sums A_hi*B_hi + A_lo*B_hi and
+// column n + CT/2 sums A_hi*B_lo + A_lo*B_lo; their fp32 sum is the product
+// (A_hi + A_lo)(B_hi + B_lo), i.e. each operand carries 22 significant bits
+// instead of tf32's 11 (the 3xTF32 scheme, with the A_lo*B_lo term kept
+// because it rides in the same instructions).
 template <int KIND>
 struct OpKind;
 template <>
 struct OpKind<0> {
   static constexpr int kElemBytes = 4;
   static constexpr uint32_t kFmt = 2;  // TF32
+  static constexpr int kHiLo = 1;
 };
 template <>
 struct OpKind<1> {
   static constexpr int kElemBytes = 2;
   static constexpr uint32_t kFmt = 1;  // BF16
+  static constexpr int kHiLo = 1;
 };
 template <>
 struct OpKind<2> {
   static constexpr int kElemBytes = 2;
   static constexpr uint32_t kFmt = 0;  // F16
+  static constexpr int kHiLo = 1;
+};
+template <>
+struct OpKind<3> {
+  static constexpr int kElemBytes = 4;
+  static constexpr uint32_t kFmt = 2;  // TF32 (hi and lo halves)
+  static constexpr int kHiLo = 2;
 };
 
 // Instruction descriptor: D fp32, A/B K-major, no negation/sparsity.
@@ -210,7 +257,7 @@ __host__ __device__ constexpr uint32_t idesc(int M, int N) {
 
 template <int KIND>
 __device__ __forceinline__ void mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t id, uint32_t acc) {
-  if constexpr (KIND == 0) {
+  if constexpr (OpKind<KIND>::kFmt == 2) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
@@ -244,11 +291,24 @@ __device__ __forceinline__ uint32_t sw128_offset(int row, int k, int rows) {
   return (uint32_t)(slice * rows * 128 + row * 128 + (((chunk ^ (row & 7)) << 4) | (byte & 15)));
 }
 
-// Store one activation value with the rounding its operand kind needs.
+__device__ __forceinline__ uint32_t rna_tf32(float v) {
+  uint32_t t;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(v));
+  return t;
+}
+
+// Store one activation value with the rounding its operand kind needs.  `rows`
+// is the buffer's row count per K slice (the MMA N); for the split kind the
+// value's hi half goes to `row` and its lo half to `row + rows / 2`.
 template <int KIND>
 __device__ __forceinline__ void store_operand(uint8_t* buf, int row, int k, int rows, float v) {
   uint8_t* p = buf + sw128_offset<KIND>(row, k, rows);
-  if constexpr (KIND == 0) {
+  if constexpr (KIND == 3) {
+    const uint32_t hi = rna_tf32(v);
+    const uint32_t lo = rna_tf32(v - __uint_as_float(hi));
+    *reinterpret_cast<uint32_t*>(p) = hi;
+    *reinterpret_cast<uint32_t*>(buf + sw128_offset<KIND>(row + rows / 2, k, rows)) = lo;
+  } else if constexpr (KIND == 0) {
     uint32_t t;
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(v));
     *reinterpret_cast<uint32_t*>(p) = t;

@@ -9,7 +9,14 @@
  *     host_* are host pointers; sizes are in elements unless named *_bytes;
  *   - `stream` is a cudaStream_t passed as void*; work is stream-ordered and
  *     nothing synchronises the device.  Calls that return host data
- *     synchronise only `stream`.
+ *     (boa_rc_get_*, boa_model_status) and boa_rc_encode_noalloc synchronise
+ *     only `stream`; every other call only enqueues work.
+ *   - errors found on the device (a bounded wait that timed out, a stream that
+ *     outgrew its pitch, a symbol outside the vocabulary) cannot be returned
+ *     by the call that enqueued the work: they are recorded on the device and
+ *     reported by the next host-returning call on the same object
+ *     (boa_rc_get_sizes / boa_rc_get_words for a coder, boa_model_status for
+ *     a model).
  *   - no torch or C++ types cross this boundary.
  *
  * Reference interfaces replaced (paths relative to the reference project root):
@@ -50,6 +57,9 @@ extern "C" {
 #define BOA_WEIGHTS_TF32 0  /* fp32 weights, tf32 tensor-core products, fp32 accumulation */
 #define BOA_WEIGHTS_BF16 1  /* bf16 weights and activations, fp32 accumulation and state */
 #define BOA_WEIGHTS_F16 2   /* fp16 weights and activations (tf32-equal mantissa), fp32 accumulation and state */
+#define BOA_WEIGHTS_TF32X3 3 /* fp32 weights and activations, each split into tf32 hi + lo halves whose
+                                products are summed in fp32 (3xTF32): the fp32-equivalent kind, and the
+                                one that matches the reference's fp32 nn.Linear (model.py:47-56,90-95) */
 
 BOA_API const char* boa_last_error(void);
 BOA_API int boa_abi_version(void);
@@ -111,17 +121,20 @@ BOA_API int boa_rc_decode_steps(boa_rc_batch* b, int n_steps, int period, const 
                                 int64_t mask_stride, void* stream);
 
 /* Allocation-free whole-stream encode (no counterpart in the reference).
- * For callers that cannot allocate device memory while they code (work being
- * captured into a CUDA graph, hosts that forbid allocation after start-up):
- * codes n_steps symbols of each of n_streams streams with the BQ quantiser,
- * then finalises, using a static per-device scratch array (2 MiB) for the
- * coder state instead of memory from boa_rc_create.  d_logits is
- * [n_steps][n_streams][K] fp32, d_symbols [n_steps][n_streams] int32, d_mask
- * [n_steps][n_streams] u8 or NULL; writes d_words [n_streams][pitch_words] and
- * d_sizes[n_streams].  At most 65536 streams (BOA_ERR_ARG beyond).  Calls
- * share the scratch: calls that overlap on the GPU race.  The first call on a
- * device looks up the scratch address; make it before any stream capture.
- * Synchronises `stream` to report overflow. */
+ * For callers that cannot allocate device memory while they code: hosts and
+ * plugin frameworks that own the device memory pool and forbid allocation
+ * after start-up, or real-time services that must not stall on cudaMalloc.
+ * Codes n_steps symbols of each of n_streams streams with the BQ quantiser,
+ * then finalises, using a static per-device scratch array (2 MiB, held by
+ * every GPU that loads the library until exit) for the coder state instead of
+ * memory from boa_rc_create.  d_logits is [n_steps][n_streams][K] fp32 (rows
+ * 16-byte aligned when K is 256 or 1024), d_symbols [n_steps][n_streams]
+ * int32, d_mask [n_steps][n_streams] u8 or NULL; writes d_words
+ * [n_streams][pitch_words] and d_sizes[n_streams].  At most 65536 streams
+ * (BOA_ERR_ARG beyond).  Calls share the scratch: calls that overlap on the
+ * GPU race.  The first call on a device looks up the scratch address.  Each
+ * call ends by reading the scratch's error word back, so it synchronises
+ * `stream` (and reports BOA_ERR_OVERFLOW / BOA_ERR_ARG found on the device). */
 BOA_API int boa_rc_encode_noalloc(int n_streams, int k_symbols, int n_steps, int precision,
                                   const float* d_logits, const int32_t* d_symbols, const uint8_t* d_mask,
                                   uint32_t* d_words, int pitch_words, int32_t* d_sizes, void* stream);
@@ -151,6 +164,15 @@ BOA_API size_t boa_model_workspace_bytes(const boa_model* m, int n_chunks);
  * bit for bit the same either way.  No reference counterpart: the reference
  * codec (codec.py:56-79) always steps one position at a time. */
 BOA_API int boa_model_set_time_block(boa_model* m, int positions);
+
+/* Wait for `stream`, then report (and clear) the device-side errors of the
+ * model's calls enqueued so far: BOA_ERR_TIMEOUT, BOA_ERR_OVERFLOW (a coded
+ * stream outgrew pitch_words), BOA_ERR_ARG (an encoded symbol outside the
+ * vocabulary).  The error bits are one word per model, shared by the calls of
+ * every stream; call this after the calls whose results you read.  Replaces
+ * the unchecked per-launch cudaDeviceSynchronize of the reference coder
+ * (gpu_range_coder.py:271,276,296,304). */
+BOA_API int boa_model_status(boa_model* m, void* stream);
 
 /* Reference-shaped single step: the streaming state of init_stream/step
  * (model.py:104-117) lives in d_workspace (zero it to start a stream).
@@ -184,17 +206,41 @@ BOA_API int boa_codec_decode(boa_model* m, int n_chunks, const uint32_t* d_words
                              uint8_t* d_out, int64_t out_pitch, int precision, void* d_workspace,
                              size_t workspace_bytes, void* stream);
 
+/* Position ranges (no counterpart in the reference, whose loops always run a
+ * chunk from its first byte to its last, codec.py:56-79,125-143): code only
+ * positions [pos_begin, pos_end) of every chunk (clipped to d_lens), with the
+ * model's recurrent state carried in d_workspace from the previous range, so
+ * a long chunk can be coded in several bounded launches.  pos_begin = 1
+ * starts from zero state; otherwise the workspace must hold the state the
+ * call for the range ending at pos_begin left there (same chunks, same
+ * workspace).  The probabilities are bit for bit those of one whole-chunk
+ * call; the coder is flushed at the end of every range, so each range is its
+ * own bitstream (d_words / d_sizes per range).  Byte rows cover positions
+ * [pos_begin - 1, pos_end): encode reads the byte before the range from slot
+ * 0 of each d_bytes row; decode takes it from d_prev_bytes[i] (the chunk's
+ * first byte when pos_begin = 1), writes it to slot 0 of each d_out row and
+ * the decoded position p to slot p - pos_begin + 1.  boa_codec_encode /
+ * boa_codec_decode are the ranges [1, INT32_MAX). */
+BOA_API int boa_codec_encode_range(boa_model* m, int n_chunks, const uint8_t* d_bytes, int64_t in_pitch,
+                                   const int32_t* d_lens, int pos_begin, int pos_end, uint32_t* d_words,
+                                   int pitch_words, int32_t* d_sizes, int precision, void* d_workspace,
+                                   size_t workspace_bytes, void* stream);
+BOA_API int boa_codec_decode_range(boa_model* m, int n_chunks, const uint32_t* d_words, int pitch_words,
+                                   const int32_t* d_sizes, const int32_t* d_lens, int pos_begin, int pos_end,
+                                   const uint8_t* d_prev_bytes, uint8_t* d_out, int64_t out_pitch, int precision,
+                                   void* d_workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Diagnostics (no reference counterpart).                                  */
 /* ------------------------------------------------------------------------ */
-/* One CTA of the model kernel's projection pipeline on host data:
- * out[M][16] = W[M][K] . X[16][K]^T with W packed into the kernel's SW128 tiles
- * (weight_format as for boa_model_create).  Synchronous; allocates scratch. */
 /* Failure-path check (no reference counterpart): launches one thread that
  * waits on a barrier nothing arrives at, with the same bounded wait every
  * kernel of the library uses.  Returns BOA_ERR_TIMEOUT once budget_cycles SM
  * cycles have passed; the CUDA context stays usable.  Synchronous. */
 BOA_API int boa_diag_timeout(int64_t budget_cycles, int device);
+/* One CTA of the model kernel's projection pipeline on host data:
+ * out[M][16] = W[M][K] . X[16][K]^T with W packed into the kernel's SW128 tiles
+ * (weight_format as for boa_model_create).  Synchronous; allocates scratch. */
 BOA_API int boa_diag_gemm(int weight_format, int M, int K, const float* h_w, const float* h_x, float* h_out,
                           int device);
 
