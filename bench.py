@@ -2,24 +2,35 @@
 """Benchmark of the BoaConstrictor compress/decompress hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
+                    [--segment S] [--scaling weak|strong] [--weights tf32x3|tf32|fp16|bf16]
 
-A step is one full pass of the hot path over one batch of synthetic input:
-compress every chunk of the configuration's input, then decompress it again
-(the round trip is verified on the first warm-up step).  Default workload is
-configuration 2 of the benchmark spec: 64 MiB of seeded HEP-like event
-records, chunks_count = 1000, BoaConstrictor d_model 256 / 8 layers, seeded
-random init, projection operands in fp16 (the 10-bit mantissa of tf32) with
-fp32 accumulation, recurrent state and element-wise math (--weights tf32 runs
-fp32 weights through tf32 products instead).  With N ranks (torchrun, one GPU each) every rank codes its own
-1000-chunk shard of an N x 64 MiB job ("scaling": "weak"); the only
-collective is the all-reduce that gathers per-chunk lengths, outside the timed
-kernels.
+Default workload: configuration 2 of the benchmark spec -- 64 MiB of seeded
+HEP-like event records, chunks_count = 1000 (67,109 B per chunk), the
+BoaConstrictor d_model 256 / 8 layers model with seeded random init, and
+projections in the fp32-equivalent 3xTF32 operand kind (every fp32 weight and
+activation split into tf32 hi + lo halves, products summed in fp32; the
+reference model is fp32 nn.Linear).  Recurrent state, element-wise math and
+accumulation are fp32.
+
+A step is one pass of the hot path over one batch: compress, then
+decompress, positions [a, a + S) of every chunk of the input (S = --segment,
+4096 by default), with each side's recurrent model state carried on the
+device from the previous step (boa_codec_encode_range / decode_range; each
+segment is its own bitstream).  Consecutive steps walk through the chunks and
+start over at position 1 after the last, so the timed steps code the
+configuration's own input, a bounded launch at a time.  The first warm-up
+steps are checked for a lossless round trip, and so is every timed step.
+
+With N ranks (torchrun, one GPU each) --scaling weak (default) gives every
+rank its own copy of the workload (an N x 64 MiB job); --scaling strong splits
+the configuration's chunks into N contiguous shares.  No collective touches
+the data path: the device times are max-reduced once, after the timed region.
 
 ``value`` is the whole-job round-trip throughput with inputs resident in HBM:
-N x bytes / max over ranks of (compress + decompress) device time, in MiB/s
-(2^20 B/s, the unit the reference's C++ port prints, boa.cpp:39).  ``e2e`` is
-the same through the public host API (codec.compress_GPU / decompress_GPU:
-pinned host bytes in, host word lists out, and back).
+bytes of all ranks / max over ranks of (compress + decompress) device time,
+in MiB/s (2^20 B/s, the unit of the reference's C++ port, boa.cpp:39).
+``e2e`` is the same through the public host API (codec.RangeCodec: pinned
+host bytes in, host words out, host words in, host bytes out, every step).
 
 ``--impl reference`` times the reference algorithm's CPU restatement
 (oracle/codec_oracle.py: fp32 model + softmax + the reference coder at
@@ -45,11 +56,11 @@ MiB = 1 << 20
 
 CONFIGS = {
     1: dict(name="config1 markov 1 MiB, chunks_count=16, d_model=64, num_layers=2", d=64, L=2, chunks=16,
-            data=("markov", 1 << 20), fmt="tf32"),
+            data=("markov", 1 << 20), fmt="tf32x3"),
     2: dict(name="config2 hep-records 64 MiB, chunks_count=1000, d_model=256, num_layers=8", d=256, L=8,
-            chunks=1000, data=("hep", 64 * MiB), fmt="fp16"),
+            chunks=1000, data=("hep", 64 * MiB), fmt="tf32x3"),
     3: dict(name="config3 hep-records 64 MiB, chunks_count=8192, d_model=256, num_layers=8", d=256, L=8,
-            chunks=8192, data=("hep", 64 * MiB), fmt="fp16"),
+            chunks=8192, data=("hep", 64 * MiB), fmt="tf32x3"),
     4: dict(name="config4 records + CFD field 1 GiB, chunks_count=65536, d_model=512, num_layers=16, bf16",
             d=512, L=16, chunks=65536, data=("mixed", 1 << 30), fmt="bf16"),
     5: dict(name="config5 range coder only, 16384 streams x 65536 symbols, logits N(0, 3^2), BQ 2^16",
@@ -64,7 +75,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--weights", default=None, choices=["tf32", "fp16", "bf16"])
+    ap.add_argument("--weights", default=None, choices=["tf32x3", "tf32", "fp16", "bf16"])
+    ap.add_argument("--segment", type=int, default=4096, help="positions of every chunk coded per step")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     ap.add_argument("--size", type=int, default=None, help="override input bytes (testing)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -170,23 +183,46 @@ def measured_peak():
         return 6650.0, "fallback 6.65 TB/s"
 
 
-def traffic_per_coded_byte(d, L, key="k_boa_step"):
-    """ncu DRAM bytes per coded byte of a kernel (k_boa_step: one position per
-    step; k_boa_step_tb4: time blocks of 4), for the model shape the capture
-    was taken on (None for other shapes)."""
+def measured_tensor_peak(fmt):
+    """Dense tensor peak for the operand kind: the measured cuBLAS bf16 burst
+    figure (MEASURED_PEAKS.json), halved for tf32 operands."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        bf16 = float(json.load(open(p))["bf16_tflops"])
+        src = "measured bf16 (MEASURED_PEAKS.json bf16_tflops)"
+    except Exception:
+        bf16, src = 1590.0, "fallback 1.59 PFLOP/s bf16"
+    if fmt in ("tf32", "tf32x3"):
+        return bf16 / 2, src + ", halved for tf32 operands"
+    return bf16, src
+
+
+def traffic_per_coded_byte(d, L, fmt, launch):
+    """ncu DRAM bytes per coded byte of the decode or encode launch, for the
+    model shape and operand kind the capture was taken on (None otherwise)."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     try:
-        rec = json.load(open(p))[key]
-        if rec.get("model", {}) != {"d_model": d, "num_layers": L}:
-            return None
-        return float(rec["dram_bytes_per_coded_byte"])
+        for rec in json.load(open(p)).values():
+            if (rec.get("model") == {"d_model": d, "num_layers": L} and rec.get("weights") == fmt
+                    and rec.get("launch") == launch):
+                return float(rec["dram_bytes_per_coded_byte"])
     except Exception:
-        return None
+        pass
+    return None
 
 
 # ---------------------------------------------------------------------------
+def gemm_macs_per_byte(d, L, V=256):
+    """Projection multiply-adds per coded byte (in_proj, x_proj, dt_proj,
+    out_proj, ff.0, ff.2 per layer; head.0, head.2)."""
+    E, R = 2 * d, (d + 15) // 16
+    return L * (d * 2 * E + E * (R + 32) + R * E + E * d + 8 * d * d) + d * d + V * d
+
+
 def cpu_baseline(cfg, arr, lens, seconds_target=20.0):
-    """The reference algorithm's CPU restatement on a bounded sample."""
+    """The reference algorithm's CPU restatement on a bounded sample (the
+    first L_s bytes of the first n_s chunks).  Returns the baseline record and
+    the sample, so the GPU path can code the very same bytes."""
     import numpy as np
     import torch
     from model import seeded_model
@@ -200,8 +236,8 @@ def cpu_baseline(cfg, arr, lens, seconds_target=20.0):
     t0 = time.perf_counter()
     co.compress(sd, chunks)
     dt = time.perf_counter() - t0
-    L_s = int(max(64, min(arr.shape[1], L_s * (seconds_target / 2) / max(dt, 1e-3))))
-    chunks = [arr[i, :L_s] for i in range(n_s)]
+    L_s = int(max(64, min(min(lens[:n_s]), L_s * (seconds_target / 2) / max(dt, 1e-3))))
+    chunks = [arr[i, :L_s].copy() for i in range(n_s)]
     t0 = time.perf_counter()
     comp, first, ls = co.compress(sd, chunks)
     t1 = time.perf_counter()
@@ -209,10 +245,11 @@ def cpu_baseline(cfg, arr, lens, seconds_target=20.0):
     t2 = time.perf_counter()
     assert all(np.array_equal(a, b) for a, b in zip(out, chunks))
     nbytes = n_s * L_s
-    return {"value": nbytes / MiB / (t2 - t0), "unit": "MiB/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{n_s} chunks x first {L_s} bytes of the workload's chunks, compress + decompress",
-            "compress_MiBps": nbytes / MiB / (t1 - t0), "decompress_MiBps": nbytes / MiB / (t2 - t1),
-            "bits_per_byte": 32.0 * sum(len(c) for c in comp) / nbytes}
+    rec = {"value": nbytes / MiB / (t2 - t0), "unit": "MiB/s", "cores": torch.get_num_threads(), "kind": "port",
+           "sample": f"{n_s} chunks x first {L_s} bytes of the workload's chunks, compress + decompress",
+           "compress_MiBps": nbytes / MiB / (t1 - t0), "decompress_MiBps": nbytes / MiB / (t2 - t1),
+           "bits_per_byte": 32.0 * sum(len(c) for c in comp) / nbytes}
+    return rec, chunks, 32 * sum(len(c) for c in comp)
 
 
 def run_reference(args, cfg, rank):
@@ -242,7 +279,7 @@ def run_reference(args, cfg, rank):
     v = args.steps * nbytes / MiB / t
     line = {"impl": "reference", "metric": "compress+decompress round-trip throughput", "value": v,
             "unit": "MiB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000 * t / args.steps, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": 1000 * t / args.steps, "higher_is_better": True, "scaling": args.scaling,
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": cfg["name"], "sample": f"{n_s} chunks x {L_s} bytes per step"},
             "cpu_baseline": {"value": v, "unit": "MiB/s", "cores": torch.get_num_threads(), "kind": "port",
@@ -251,135 +288,211 @@ def run_reference(args, cfg, rank):
     print(json.dumps(line), flush=True)
 
 
+DTYPES = {"tf32x3": "f32 (3xTF32: tf32 hi + lo operand halves, fp32 accumulation)",
+          "tf32": "tf32 products / f32", "fp16": "fp16 products / f32", "bf16": "bf16 products / f32"}
+
+
 # ---------------------------------------------------------------------------
 def run_ours(args, cfg, rank, world, local_rank, dist):
     import numpy as np
     import torch
     import codec
     from model import seeded_model
+    from boa_b200.shard import shard_range
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     fmt = args.weights or cfg["fmt"]
     data = make_data(cfg, args.size)
     arr, lens = chunk_array(data, cfg["chunks"])
+    n_all = arr.shape[0]
+    if args.scaling == "strong" and world > 1:
+        lo, hi = shard_range(n_all, world, rank)
+        arr, lens = arr[lo:hi], lens[lo:hi]
     n, maxL = arr.shape
-    nbytes = int(sum(lens))
+    total_bytes = int(sum(lens))
     model = seeded_model(cfg["d"], cfg["L"], weight_format=fmt)
     nm = model.native(dev)
     X = torch.from_numpy(arr).to(dev)
     Ld = torch.tensor(lens, dtype=torch.int32, device=dev)
+    lens_np = np.asarray(lens, np.int64)
     first = X[:, 0].contiguous()
-    ws = torch.empty(nm.workspace_bytes(n), dtype=torch.uint8, device=dev)
+    ws_e = torch.empty(nm.workspace_bytes(n), dtype=torch.uint8, device=dev)
+    ws_d = torch.empty_like(ws_e)
+    out = torch.zeros((n, maxL), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
+    S = max(1, args.segment)
+    segs = [(a, min(a + S, maxL)) for a in range(1, max(maxL, 2), S)]
+    nseg = len(segs)
+
+    def seg_bytes(k):
+        """Input bytes a step over segment k accounts for: its coded
+        positions, plus the raw first byte of every chunk for segment 0."""
+        a, b = segs[k]
+        coded = int(np.clip(np.minimum(lens_np, b) - a, 0, None).sum())
+        return coded + (n if a == 1 else 0)
+
+    def step(k):
+        a, b = segs[k % nseg]
+        words, sizes = codec.encode_device(model, X, Ld, workspace=ws_e, pos_begin=a, pos_end=b)
+        e_mid = torch.cuda.Event(enable_timing=True)
+        e_mid.record(stream)
+        codec.decode_device(model, words, sizes, Ld, first, workspace=ws_d, pos_begin=a, pos_end=b, out=out)
+        return sizes, e_mid
+
+    def verify(upto):
+        """Decoded bytes equal the input for positions < upto."""
+        mask = torch.arange(maxL, device=dev)[None, :] < torch.minimum(Ld, torch.tensor(upto, device=dev))[:, None]
+        if not torch.equal(out[mask], X[mask]):
+            raise RuntimeError("round trip mismatch")
 
     def barrier():
         if dist is not None:
             dist.barrier()
 
-    # warm-up (first one verifies the round trip)
-    comp_bits = None
+    # warm-up: the first W segments of a separate pass, checked
     for w in range(max(args.warmup, 1)):
-        words, sizes = codec.encode_device(model, X, Ld, workspace=ws)
-        out = codec.decode_device(model, words, sizes, Ld, first, max_len=maxL, workspace=ws)
-        if w == 0:
-            torch.cuda.synchronize(dev)
-            mask = torch.arange(maxL, device=dev)[None, :] < Ld[:, None]
-            if not torch.equal(out[mask], X[mask]):
-                raise RuntimeError("round trip mismatch")
-            comp_bits = int(sizes.to(torch.int64).sum().item()) * 32
+        step(w)
+    nm.check()
+    verify(segs[min(max(args.warmup, 1), nseg) - 1][1])
 
     # timed device-resident region
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    out.zero_()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    mids, sizes_l = [], []
     barrier()
     torch.cuda.synchronize(dev)
     with ClockSampler(local_rank) as clk:
         for k in range(args.steps):
-            e0, e1, e2 = ev[k]
-            e0.record(stream)
-            words, sizes = codec.encode_device(model, X, Ld, workspace=ws)
-            e1.record(stream)
-            out = codec.decode_device(model, words, sizes, Ld, first, max_len=maxL, workspace=ws)
-            e2.record(stream)
+            ev[k][0].record(stream)
+            sz, e_mid = step(k)
+            ev[k][1].record(stream)
+            mids.append(e_mid)
+            sizes_l.append(sz)
         torch.cuda.synchronize(dev)
     barrier()
-    t_c = sum(e0.elapsed_time(e1) for e0, e1, _ in ev) / 1000.0
-    t_d = sum(e1.elapsed_time(e2) for _, e1, e2 in ev) / 1000.0
+    nm.check()
+    verify(segs[min(args.steps, nseg) - 1][1] if args.steps < nseg else maxL)
+    t_c = sum(ev[k][0].elapsed_time(mids[k]) for k in range(args.steps)) / 1000.0
+    t_d = sum(mids[k].elapsed_time(ev[k][1]) for k in range(args.steps)) / 1000.0
+    step_bytes = [seg_bytes(k % nseg) for k in range(args.steps)]
+    bytes_timed = sum(step_bytes)
+    coded_timed = sum(b - (n if segs[k % nseg][0] == 1 else 0) for k, b in enumerate(step_bytes))
+    words_timed = sum(int(sz.to(torch.int64).sum().item()) for sz in sizes_l)
     tt = torch.tensor([t_c + t_d, t_c, t_d], dtype=torch.float64, device=dev)
     if dist is not None:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     t_tot, t_c, t_d = (float(x) for x in tt.cpu())
-    value = world * args.steps * nbytes / MiB / t_tot
+    # every rank codes the same amount (weak) or its share (strong): sum over ranks
+    bt = torch.tensor([bytes_timed], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(bt)
+    job_bytes = float(bt.item())
+    value = job_bytes / MiB / t_tot
 
-    # end-to-end through the host API
+    # end-to-end through the public host API, from pinned host segments
     e2e = None
     if not args.no_e2e:
-        xs = [torch.from_numpy(arr[i:i + 1, :lens[i]]) for i in range(n)]
+        rcod = codec.RangeCodec(model, lens, arr[:, 0], device=dev)
+        host_segs = []
+        for k in range(min(args.steps, nseg)):
+            a, b = segs[k]
+            hseg = torch.zeros((n, b - a + 1), dtype=torch.uint8).pin_memory()
+            hseg.numpy()[:] = arr[:, a - 1:b]
+            host_segs.append(hseg)
+        h2d = d2h = 0
+        outs = []
         barrier()
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
-        h2d = d2h = 0
         for k in range(args.steps):
-            comp, fb, ls = codec.compress_GPU(model, xs, device=dev)
-            outs = codec.decompress_GPU(model, comp, ls, fb, device=dev)
-            h2d += nbytes + sum(4 * len(c) for c in comp)
-            d2h += sum(4 * len(c) for c in comp) + nbytes
+            a, b = segs[k % nseg]
+            w_h, s_h = rcod.encode(host_segs[k % nseg], a, b)
+            o_h = rcod.decode(w_h, s_h, a, b)
+            h2d += host_segs[k % nseg].numel() + w_h.nbytes + s_h.nbytes
+            d2h += w_h.nbytes + s_h.nbytes + o_h.nbytes
+            if k < nseg:
+                outs.append(o_h)
         torch.cuda.synchronize(dev)
         te = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
         if dist is not None:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        if not all(np.array_equal(o[0], arr[i, :lens[i]]) for i, o in enumerate(outs)):
-            raise RuntimeError("e2e round trip mismatch")
-        e2e = {"value": world * args.steps * nbytes / MiB / float(te.item()), "unit": "MiB/s",
-               "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps}
+        for k, o_h in enumerate(outs):
+            a, b = segs[k]
+            ref = arr[:, a:b].copy()
+            ref[np.arange(b - a)[None, :] >= (lens_np - a)[:, None]] = 0
+            if not np.array_equal(o_h, ref):
+                raise RuntimeError("e2e round trip mismatch")
+        e2e = {"value": job_bytes / MiB / float(te.item()), "unit": "MiB/s",
+               "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps,
+               "api": "codec.RangeCodec.encode / decode (pinned host segments in, host words and bytes out)"}
         barrier()
 
     if rank != 0:
         return
-    coded = sum(max(x - 1, 0) for x in lens)
     sb = state_bytes_per_coded_byte(cfg["d"], cfg["L"])
     peak, peak_src = measured_peak()
-    tpb = traffic_per_coded_byte(cfg["d"], cfg["L"])
+    tpb = traffic_per_coded_byte(cfg["d"], cfg["L"], fmt, "decode")
     # dominant kernel: the decode launch (one position per kernel step)
-    alg_d = sb * coded + nbytes + comp_bits // 8
-    ach_d = alg_d / (t_d / args.steps) / 1e9
+    alg_d = sb * coded_timed + bytes_timed + 4 * words_timed
+    ach_d = alg_d / t_d / 1e9
     roof = {"bound": "hbm", "kernel": "k_boa_step decode launch (fused model+quantiser+coder, one position per step)",
             "achieved": ach_d, "peak": peak, "unit": "GB/s", "frac": ach_d / peak, "peak_source": peak_src,
-            "traffic": (tpb * coded if tpb else None),
-            "algorithmic_bytes_per_launch": alg_d,
+            "traffic": (tpb * coded_timed / args.steps if tpb else None),
+            "algorithmic_bytes_per_launch": alg_d / args.steps,
             "per_unit": f"{sb} B recurrent-state read+write per coded byte"}
     # encode launch: time blocks of 4 positions read and write the state once per block
     tb = 4
-    alg_c = sb * coded // tb + nbytes + comp_bits // 8
-    ach_c = alg_c / (t_c / args.steps) / 1e9
-    tpb_c = traffic_per_coded_byte(cfg["d"], cfg["L"], "k_boa_step_tb4")
+    alg_c = sb * coded_timed // tb + bytes_timed + 4 * words_timed
+    ach_c = alg_c / t_c / 1e9
+    tpb_c = traffic_per_coded_byte(cfg["d"], cfg["L"], fmt, "encode")
     roof_c = {"bound": "hbm", "kernel": "k_boa_step encode launch (time blocks of 4 positions)",
               "achieved": ach_c, "peak": peak, "unit": "GB/s", "frac": ach_c / peak,
-              "traffic": (tpb_c * coded if tpb_c else None),
-              "algorithmic_bytes_per_launch": alg_c,
+              "traffic": (tpb_c * coded_timed / args.steps if tpb_c else None),
+              "algorithmic_bytes_per_launch": alg_c / args.steps,
               "per_unit": f"{sb // tb} B recurrent-state read+write per coded byte"}
-    cpu = None
+    # tensor pipe: the model's projection FLOPs, and what the split kind issues
+    macs = gemm_macs_per_byte(cfg["d"], cfg["L"])
+    products = 4 if fmt == "tf32x3" else 1
+    tf_peak, tf_src = measured_tensor_peak(fmt)
+    fl_d = 2.0 * macs * coded_timed * products / t_d / 1e12
+    roof_t = {"bound": "tensor", "kernel": "k_boa_step decode launch, projections",
+              "achieved": fl_d, "peak": tf_peak, "unit": "TFLOP/s", "frac": fl_d / tf_peak, "peak_source": tf_src,
+              "per_unit": f"{2 * macs} model FLOP per coded byte x {products} tensor products per multiply "
+                          f"({fmt})"}
+    cpu, size_ref = None, None
     if world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(cfg, arr, lens)
+        cpu, sample, ref_bits = cpu_baseline(cfg, arr, lens)
+        xs = [torch.from_numpy(c).reshape(1, -1) for c in sample]
+        comp, _, _ = codec.compress_GPU(model, xs, device=dev)
+        gpu_bits = 32 * sum(len(c) for c in comp)
+        size_ref = {"ratio": gpu_bits / ref_bits, "bits_gpu": gpu_bits, "bits_reference_path": ref_bits,
+                    "sample": cpu["sample"].replace(", compress + decompress", ""),
+                    "reference_path": "fp32 model, softmax, build_cdf_fast at PRECISION 24, reference range coder "
+                                      "(oracle/codec_oracle.py)",
+                    "gpu_path": f"{fmt} kernel, integer quantiser at PRECISION 16, whole-chunk streams"}
+    passes = args.steps / nseg
     line = {
         "metric": "compress+decompress round-trip throughput", "value": value, "unit": "MiB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * t_tot / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": {"tf32": "tf32 products / f32", "fp16": "fp16 products / f32",
-                                       "bf16": "bf16 products / f32"}[fmt],
+        "ms_per_step": 1000.0 * t_tot / args.steps, "higher_is_better": True, "scaling": args.scaling,
+        "vs_baseline": None, "dtype": DTYPES[fmt],
         "data": "synthetic (seeded HEP-like records, random-init seeded weights)",
-        "config": {"workload": cfg["name"], "chunks_per_gpu": n, "chunk_len": maxL, "bytes_per_gpu": nbytes,
-                   "weights": fmt, "precision": codec.PRECISION, "parallelism": f"chunk shards x{world}",
-                   "l2": "inputs larger than L2: recurrent state %d MB per pass" %
-                         (state_bytes_per_coded_byte(cfg['d'], cfg['L']) * n // 2 // 1000000)},
-        "compress_MiBps": world * args.steps * nbytes / MiB / t_c,
-        "decompress_MiBps": world * args.steps * nbytes / MiB / t_d,
-        "compress_MBps_1e6": world * args.steps * nbytes / 1e6 / t_c,
-        "decompress_MBps_1e6": world * args.steps * nbytes / 1e6 / t_d,
-        "bits_per_byte": comp_bits / nbytes,
-        "roofline": roof, "roofline_encode": roof_c, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
-        "gpu_launches": 2 * args.steps,
+        "config": {"workload": cfg["name"], "chunks_per_gpu": n, "chunk_len": maxL, "bytes_per_gpu": total_bytes,
+                   "step": f"positions [a, a + {S}) of every chunk, recurrent state carried between steps; "
+                           f"{nseg} steps make one pass over the input ({passes:.2f} passes timed)",
+                   "weights": fmt, "precision": codec.PRECISION,
+                   "parallelism": f"chunk shards x{world} ({args.scaling})",
+                   "l2": "inputs larger than L2: recurrent state %d MB per side" %
+                         (sb * n // 2 // 1000000)},
+        "compress_MiBps": job_bytes / MiB / t_c,
+        "decompress_MiBps": job_bytes / MiB / t_d,
+        "compress_MBps_1e6": job_bytes / 1e6 / t_c,
+        "decompress_MBps_1e6": job_bytes / 1e6 / t_d,
+        "bits_per_byte": 32.0 * words_timed / bytes_timed,
+        "size_vs_reference": size_ref,
+        "roofline": roof, "roofline_encode": roof_c, "roofline_tensor": roof_t, "cpu_baseline": cpu, "e2e": e2e,
+        "clocks": clk.summary(), "gpu_launches": 2 * args.steps,
     }
     print(json.dumps(line), flush=True)
 

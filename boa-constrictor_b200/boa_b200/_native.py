@@ -28,6 +28,7 @@ BOA_QUANT_BQ = 1
 BOA_WEIGHTS_TF32 = 0
 BOA_WEIGHTS_BF16 = 1
 BOA_WEIGHTS_F16 = 2
+BOA_WEIGHTS_TF32X3 = 3
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -58,12 +59,15 @@ SIGNATURES = {
     "boa_model_workspace_bytes": [_P, _I],
     "boa_model_info": [_P, _P, _P, _P, _P, _P],
     "boa_model_set_time_block": [_P, _I],
+    "boa_model_status": [_P, _P],
     "boa_diag_timeout": [_I64, _I],
     "boa_diag_gemm": [_I, _I, _I, _P, _P, _P, _I],
     "boa_model_step": [_P, _I, _P, _P, _P, _SZ, _P],
     "boa_model_logits": [_P, _I, _I, _P, _P, _P, _SZ, _P],
     "boa_codec_encode": [_P, _I, _P, _I64, _P, _P, _I, _P, _I, _P, _SZ, _P],
     "boa_codec_decode": [_P, _I, _P, _I, _P, _P, _P, _P, _I64, _I, _P, _SZ, _P],
+    "boa_codec_encode_range": [_P, _I, _P, _I64, _P, _I, _I, _P, _I, _P, _I, _P, _SZ, _P],
+    "boa_codec_decode_range": [_P, _I, _P, _I, _P, _P, _I, _I, _P, _P, _I64, _I, _P, _SZ, _P],
 }
 _RESTYPES = {
     "boa_last_error": ctypes.c_char_p,

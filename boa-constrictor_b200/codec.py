@@ -39,15 +39,28 @@ def _ws(model, dev, n):
     return nm, torch.empty(nm.workspace_bytes(n), dtype=torch.uint8, device=dev)
 
 
+INT32_MAX = (1 << 31) - 1
+
+
 @torch.inference_mode()
 def encode_device(model, X: torch.Tensor, lens: torch.Tensor, precision: int = PRECISION,
-                  pitch_words: int | None = None, workspace: torch.Tensor | None = None):
+                  pitch_words: int | None = None, workspace: torch.Tensor | None = None,
+                  pos_begin: int = 1, pos_end: int | None = None):
     """X [N, maxL] uint8 (device), lens [N] int32 (device) ->
-    (words [N, pitch] int32 view of u32, sizes [N] int32), all on the device."""
+    (words [N, pitch] int32 view of u32, sizes [N] int32), all on the device.
+
+    Codes positions [pos_begin, pos_end) of every chunk (default: all of
+    them).  A range that does not start at 1 continues from the recurrent
+    state that the previous range left in `workspace` (pass the same one); each
+    range is its own bitstream.  Only enqueues work on the current stream:
+    device-side errors surface through ``model.native(dev).check()``."""
     dev = X.device
     N, maxL = X.shape
+    stop = INT32_MAX if pos_end is None else int(pos_end)
+    if pos_begin < 1 or stop <= pos_begin:
+        raise ValueError("need 1 <= pos_begin < pos_end")
     if pitch_words is None:
-        pitch_words = pitch_words_for(maxL, precision)
+        pitch_words = pitch_words_for(max(min(stop, maxL) - pos_begin, 0) + 1, precision)
     nm = model._native_handle(dev)
     if workspace is None:
         workspace = torch.empty(nm.workspace_bytes(N), dtype=torch.uint8, device=dev)
@@ -56,35 +69,52 @@ def encode_device(model, X: torch.Tensor, lens: torch.Tensor, precision: int = P
     X = X.contiguous()
     lens = lens.to(torch.int32).contiguous()
     with torch.cuda.device(dev):
-        _n.call("boa_codec_encode", nm.h, N, ctypes.c_void_p(X.data_ptr()), ctypes.c_int64(X.stride(0)),
-                ctypes.c_void_p(lens.data_ptr()), ctypes.c_void_p(words.data_ptr()), int(pitch_words),
-                ctypes.c_void_p(sizes.data_ptr()), int(precision), ctypes.c_void_p(workspace.data_ptr()),
-                ctypes.c_size_t(workspace.numel()), ctypes.c_void_p(_n.stream_ptr(dev)))
+        # byte rows start at position pos_begin - 1 (the byte before the range)
+        _n.call("boa_codec_encode_range", nm.h, N, ctypes.c_void_p(X.data_ptr() + (pos_begin - 1)),
+                ctypes.c_int64(X.stride(0)), ctypes.c_void_p(lens.data_ptr()), int(pos_begin), int(stop),
+                ctypes.c_void_p(words.data_ptr()), int(pitch_words), ctypes.c_void_p(sizes.data_ptr()),
+                int(precision), ctypes.c_void_p(workspace.data_ptr()), ctypes.c_size_t(workspace.numel()),
+                ctypes.c_void_p(_n.stream_ptr(dev)))
     return words, sizes
 
 
 @torch.inference_mode()
 def decode_device(model, words: torch.Tensor, sizes: torch.Tensor, lens: torch.Tensor, first: torch.Tensor,
-                  max_len: int | None = None, precision: int = PRECISION, workspace: torch.Tensor | None = None):
+                  max_len: int | None = None, precision: int = PRECISION, workspace: torch.Tensor | None = None,
+                  pos_begin: int = 1, pos_end: int | None = None, out: torch.Tensor | None = None):
     """words [N, pitch] (device, u32 as int32), sizes [N] int32, lens [N] int32,
-    first [N] uint8 -> out [N, maxL] uint8 on the device."""
+    first [N] uint8 -> out [N, maxL] uint8 on the device.
+
+    With a range [pos_begin, pos_end) only those positions are decoded into
+    `out` (pass the tensor the earlier ranges filled, and the same workspace);
+    the byte before the range is read from ``out[:, pos_begin - 1]``.  Only
+    enqueues work on the current stream."""
     dev = words.device
     N, pitch = words.shape
-    if max_len is None:
-        max_len = int(lens.max().item())
+    stop = INT32_MAX if pos_end is None else int(pos_end)
+    if pos_begin < 1 or stop <= pos_begin:
+        raise ValueError("need 1 <= pos_begin < pos_end")
     nm = model._native_handle(dev)
     if workspace is None:
         workspace = torch.empty(nm.workspace_bytes(N), dtype=torch.uint8, device=dev)
-    out = torch.empty((N, max_len), dtype=torch.uint8, device=dev)
+    if out is None:
+        if max_len is None:
+            max_len = int(lens.max().item())
+        out = torch.empty((N, max_len), dtype=torch.uint8, device=dev)
+    if pos_begin == 1:
+        prev = first.to(torch.uint8).contiguous()
+    else:
+        if pos_begin - 1 >= out.shape[1]:
+            raise ValueError("pos_begin lies beyond the output rows")
+        prev = out[:, pos_begin - 1].contiguous()
     words = words.contiguous()
     with torch.cuda.device(dev):
-        _n.call("boa_codec_decode", nm.h, N, ctypes.c_void_p(words.data_ptr()), int(pitch),
+        _n.call("boa_codec_decode_range", nm.h, N, ctypes.c_void_p(words.data_ptr()), int(pitch),
                 ctypes.c_void_p(sizes.to(torch.int32).contiguous().data_ptr()),
-                ctypes.c_void_p(lens.to(torch.int32).contiguous().data_ptr()),
-                ctypes.c_void_p(first.to(torch.uint8).contiguous().data_ptr()),
-                ctypes.c_void_p(out.data_ptr()), ctypes.c_int64(out.stride(0)), int(precision),
-                ctypes.c_void_p(workspace.data_ptr()), ctypes.c_size_t(workspace.numel()),
-                ctypes.c_void_p(_n.stream_ptr(dev)))
+                ctypes.c_void_p(lens.to(torch.int32).contiguous().data_ptr()), int(pos_begin), int(stop),
+                ctypes.c_void_p(prev.data_ptr()), ctypes.c_void_p(out.data_ptr() + (pos_begin - 1)),
+                ctypes.c_int64(out.stride(0)), int(precision), ctypes.c_void_p(workspace.data_ptr()),
+                ctypes.c_size_t(workspace.numel()), ctypes.c_void_p(_n.stream_ptr(dev)))
     return out
 
 
@@ -120,6 +150,7 @@ def compress_GPU(model, x_list: list, device="cuda", progress=True, num_workers:
     words, sizes = encode_device(model, X, lens, precision=precision)
     sizes_h = sizes.cpu().numpy()
     words_h = words.cpu().numpy().view(np.uint32)
+    model._native_handle(dev).check()
     out = [words_h[i, :int(sizes_h[i])].copy() for i in range(N)]
     return out, first_bytes, Ls
 
@@ -147,6 +178,7 @@ def decompress_GPU(model, compressed_list, full_lens: list, first_bytes: list, d
     first_d = torch.tensor([int(b) & 0xFF for b in first_bytes], dtype=torch.uint8).to(dev)
     out = decode_device(model, words, sizes_d, lens_d, first_d, max_len=maxL, precision=precision)
     out_h = out.cpu().numpy()
+    model._native_handle(dev).check()
     return [out_h[i, :full_lens[i]].reshape(1, -1).copy() for i in range(N)]
 
 
@@ -156,3 +188,80 @@ def compress_CPU(*args, **kwargs):
 
 def decompress_CPU(*args, **kwargs):
     raise RuntimeError("boa_b200 has no CPU codec path; run on a CUDA device (sm_100a)")
+
+
+class RangeCodec:
+    """Codes a fixed batch of chunks in consecutive position ranges, from host
+    buffers to host buffers, carrying each side's recurrent model state on the
+    device between calls (``boa_codec_encode_range`` /
+    ``boa_codec_decode_range``).  For chunks too long to code in one launch
+    (each call is a bounded piece of work) and for streaming producers and
+    consumers.  No reference counterpart: the reference loops code a chunk
+    from its first byte to its last (codec.py:56-79,125-143).
+
+    ``encode(seg, a, b)`` takes ``seg`` [N, b - a + 1] uint8 (positions
+    [a - 1, b) of every chunk, zero padded past a chunk's end; pinned host
+    memory copies asynchronously) and returns (words [N, pitch] uint32,
+    sizes [N] int32) as numpy arrays; ``decode(words, sizes, a, b)`` returns
+    positions [a, b) of every chunk as [N, b - a] uint8.  Ranges must be
+    coded in order on each side; every range is its own bitstream."""
+
+    def __init__(self, model, lens, first_bytes, device="cuda", precision: int = PRECISION):
+        self.dev = _device(device)
+        self.model = model
+        self.precision = precision
+        self.lens_h = np.asarray(lens, dtype=np.int32)
+        self.N = len(self.lens_h)
+        self.nm = model._native_handle(self.dev)
+        self.lens = torch.from_numpy(self.lens_h).to(self.dev)
+        self.first = torch.tensor([int(b) & 0xFF for b in first_bytes], dtype=torch.uint8).to(self.dev)
+        nb = self.nm.workspace_bytes(self.N)
+        self.ws_enc = torch.empty(nb, dtype=torch.uint8, device=self.dev)
+        self.ws_dec = torch.empty(nb, dtype=torch.uint8, device=self.dev)
+        self.prev_dec = self.first.clone()
+
+    @torch.inference_mode()
+    def encode(self, seg, pos_begin: int, pos_end: int):
+        seg_t = torch.as_tensor(seg)
+        X = seg_t.to(self.dev, non_blocking=True)
+        words, sizes = _encode_range_rows(self, X, pos_begin, pos_end)
+        w_h = words.cpu().numpy().view(np.uint32)
+        s_h = sizes.cpu().numpy()
+        self.nm.check()
+        return w_h, s_h
+
+    @torch.inference_mode()
+    def decode(self, words, sizes, pos_begin: int, pos_end: int):
+        w = torch.from_numpy(np.ascontiguousarray(words).view(np.int32)).to(self.dev, non_blocking=True)
+        s = torch.from_numpy(np.ascontiguousarray(sizes, dtype=np.int32)).to(self.dev, non_blocking=True)
+        out = torch.zeros((self.N, pos_end - pos_begin + 1), dtype=torch.uint8, device=self.dev)
+        prev = self.first if pos_begin == 1 else self.prev_dec
+        with torch.cuda.device(self.dev):
+            _n.call("boa_codec_decode_range", self.nm.h, self.N, ctypes.c_void_p(w.data_ptr()), int(w.shape[1]),
+                    ctypes.c_void_p(s.data_ptr()), ctypes.c_void_p(self.lens.data_ptr()), int(pos_begin),
+                    int(pos_end), ctypes.c_void_p(prev.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                    ctypes.c_int64(out.stride(0)), int(self.precision), ctypes.c_void_p(self.ws_dec.data_ptr()),
+                    ctypes.c_size_t(self.ws_dec.numel()), ctypes.c_void_p(_n.stream_ptr(self.dev)))
+        # the byte before the next range: the last position of this one each chunk reached
+        last = torch.clamp(torch.minimum(self.lens, torch.tensor(pos_end, device=self.dev)) - pos_begin, min=0)
+        self.prev_dec = torch.where(self.lens > pos_begin - 1, out.gather(1, last.long()[:, None])[:, 0], prev)
+        out_h = out[:, 1:].cpu().numpy()
+        self.nm.check()
+        return out_h
+
+
+def _encode_range_rows(rc: "RangeCodec", X: torch.Tensor, pos_begin: int, pos_end: int):
+    """Encode positions [pos_begin, pos_end) from rows that start at position
+    pos_begin - 1 (X [N, pos_end - pos_begin + 1] on the device)."""
+    N = rc.N
+    pitch = pitch_words_for(pos_end - pos_begin + 1, rc.precision)
+    words = torch.empty((N, pitch), dtype=torch.int32, device=rc.dev)
+    sizes = torch.empty((N,), dtype=torch.int32, device=rc.dev)
+    X = X.contiguous()
+    with torch.cuda.device(rc.dev):
+        _n.call("boa_codec_encode_range", rc.nm.h, N, ctypes.c_void_p(X.data_ptr()), ctypes.c_int64(X.stride(0)),
+                ctypes.c_void_p(rc.lens.data_ptr()), int(pos_begin), int(pos_end),
+                ctypes.c_void_p(words.data_ptr()), int(pitch), ctypes.c_void_p(sizes.data_ptr()),
+                int(rc.precision), ctypes.c_void_p(rc.ws_enc.data_ptr()), ctypes.c_size_t(rc.ws_enc.numel()),
+                ctypes.c_void_p(_n.stream_ptr(rc.dev)))
+    return words, sizes

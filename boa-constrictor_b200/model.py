@@ -28,7 +28,14 @@ D_STATE = 16
 D_CONV = 4
 EXPAND = 2
 
-WEIGHT_FORMATS = {"tf32": _n.BOA_WEIGHTS_TF32, "bf16": _n.BOA_WEIGHTS_BF16, "fp16": _n.BOA_WEIGHTS_F16}
+# Projection operand formats of the kernel.  "tf32x3" (the default) splits every
+# fp32 weight and activation into tf32 hi + lo halves whose products are summed
+# in fp32: the arithmetic of the reference's fp32 nn.Linear to within fp32
+# rounding.  "tf32", "fp16" and "bf16" are faster, narrower alternatives
+# ("bf16" is what the d_model-512 configuration specifies).
+WEIGHT_FORMATS = {"tf32x3": _n.BOA_WEIGHTS_TF32X3, "tf32": _n.BOA_WEIGHTS_TF32, "bf16": _n.BOA_WEIGHTS_BF16,
+                  "fp16": _n.BOA_WEIGHTS_F16}
+DEFAULT_FORMAT = "tf32x3"
 
 
 class Mamba(nn.Module):
@@ -102,6 +109,15 @@ class NativeModel:
         """Positions per kernel step for encode / logits runs: 4 (default) or 1."""
         _n.call("boa_model_set_time_block", self.h, int(positions))
 
+    def check(self, stream=None) -> None:
+        """Wait for `stream` (torch's current stream by default) and raise the
+        device-side errors of this model's calls enqueued so far
+        (boa_model_status: timeouts, overflowing streams, bad symbols)."""
+        import torch
+        if stream is None:
+            stream = torch.cuda.current_stream(torch.device("cuda", self.device_index))
+        _n.call("boa_model_status", self.h, ctypes.c_void_p(int(stream.cuda_stream)))
+
     def tile_bytes_per_step(self) -> int:
         v = ctypes.c_size_t()
         _n.call("boa_model_info", self.h, None, None, None, None, ctypes.byref(v))
@@ -122,7 +138,7 @@ class NativeModel:
 class BoaBytePredictor(nn.Module):
     """Mamba model predicting the next byte (model.py:83-131)."""
 
-    def __init__(self, d_model=256, num_layers=4, vocab_size=256, weight_format: str = "tf32"):
+    def __init__(self, d_model=256, num_layers=4, vocab_size=256, weight_format: str = DEFAULT_FORMAT):
         super().__init__()
         self.embedding = nn.Embedding(vocab_size, d_model)
         self.blocks = nn.ModuleList([MambaBlock(d_model) for _ in range(num_layers)])
@@ -196,7 +212,7 @@ class BoaBytePredictor(nn.Module):
         return out
 
 
-def BoaConstrictor(d_model=256, num_layers=4, vocab_size=256, device="cuda", weight_format: str = "tf32"):
+def BoaConstrictor(d_model=256, num_layers=4, vocab_size=256, device="cuda", weight_format: str = DEFAULT_FORMAT):
     """Construct a BoaBytePredictor (model.py:5-134).  Parameters are created on
     the CPU with the module-construction order of the reference (embedding,
     blocks, head) so a given torch seed always yields the same weights; the
@@ -212,7 +228,7 @@ def BoaConstrictor(d_model=256, num_layers=4, vocab_size=256, device="cuda", wei
 
 
 def seeded_model(d_model: int, num_layers: int, vocab_size: int = 256, seed: int = 0,
-                 weight_format: str = "tf32") -> BoaBytePredictor:
+                 weight_format: str = DEFAULT_FORMAT) -> BoaBytePredictor:
     """The benchmark/test model: torch.manual_seed(seed) then construction."""
     torch.manual_seed(seed)
     return BoaConstrictor(d_model=d_model, num_layers=num_layers, vocab_size=vocab_size, device="cpu",

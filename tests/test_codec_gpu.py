@@ -13,7 +13,7 @@ from oracle import model_oracle as mo
 pytestmark = pytest.mark.gpu
 
 
-def _model(d=64, L=2, fmt="tf32"):
+def _model(d=64, L=2, fmt="tf32x3"):
     from model import seeded_model
     return seeded_model(d, L, weight_format=fmt)
 
@@ -23,7 +23,7 @@ def _chunks(seed, lens, alphabet=256):
     return [torch.from_numpy(rng.integers(0, alphabet, (1, n)).astype(np.uint8)) for n in lens]
 
 
-@pytest.mark.parametrize("fmt", ["tf32", "fp16"])
+@pytest.mark.parametrize("fmt", ["tf32x3", "tf32", "fp16"])
 def test_roundtrip_ragged(fmt):
     import codec
     m = _model(fmt=fmt)
@@ -127,8 +127,11 @@ def test_pitch_overflow_is_an_error():
     m = _model()
     x = torch.randint(0, 256, (4, 500), dtype=torch.uint8).cuda()
     lens = torch.full((4,), 500, dtype=torch.int32).cuda()
-    with pytest.raises(BoaError):
+    with pytest.raises(BoaError) as ei:
         codec.encode_device(m, x, lens, pitch_words=8)
+        m.native(x.device).check()               # device-side errors surface at the status call
+    assert ei.value.code == 3                    # BOA_ERR_OVERFLOW
+    m.native(x.device).check()                   # and are cleared once reported
 
 
 def test_roundtrip_d256_split_and_single():
@@ -147,7 +150,7 @@ def test_roundtrip_d256_split_and_single():
     assert all(np.array_equal(a, b) for a, b in zip(comp, comp2[:40]))
 
 
-@pytest.mark.parametrize("d,fmt", [(64, "tf32"), (256, "fp16")])
+@pytest.mark.parametrize("d,fmt", [(64, "tf32"), (256, "fp16"), (64, "tf32x3"), (256, "tf32x3")])
 def test_time_blocked_encode_matches_one_position_steps(d, fmt):
     """Encode in time blocks of 4 positions (the default) writes the same
     words as encode one position per kernel step, for lengths that end at
@@ -209,3 +212,53 @@ def test_roundtrip_d512_bf16():
     comp, first, Ls = codec.compress_GPU(m, xs)
     outs = codec.decompress_GPU(m, comp, Ls, first)
     assert all(np.array_equal(x.numpy(), o) for x, o in zip(xs, outs))
+
+
+@pytest.mark.parametrize("d,L,fmt", [(64, 2, "tf32x3"), (256, 2, "tf32x3"), (256, 2, "fp16")])
+def test_position_ranges_continue_the_model_state(d, L, fmt):
+    """Coding [1, a), [a, b), [b, end) as three launches that carry the
+    recurrent state in one workspace uses exactly the probabilities of one
+    whole-chunk launch: each range's words equal the CPU oracle coder run on
+    the whole-sequence logits of that range's positions, and decoding the
+    ranges in the same order restores every chunk.  Boundaries fall inside
+    and at the edges of 4-position time blocks, and past some chunks' ends."""
+    import codec
+    m = _model(d, L, fmt)
+    dev = torch.device("cuda", 0)
+    lens = [1, 5, 37, 70, 71, 96, 129, 130, 200] * 4
+    xs = _chunks(21, lens)
+    N, maxL = len(lens), max(lens)
+    host = np.zeros((N, maxL), np.uint8)
+    for i, x in enumerate(xs):
+        host[i, :lens[i]] = x.numpy()[0]
+    X = torch.from_numpy(host).to(dev)
+    Ld = torch.tensor(lens, dtype=torch.int32, device=dev)
+    lg = m(X.long()).cpu().numpy()                        # whole-sequence logits (next-byte)
+    nm = m.native(dev)
+    ws_e = torch.empty(nm.workspace_bytes(N), dtype=torch.uint8, device=dev)
+    ws_d = torch.empty_like(ws_e)
+    bounds = [1, 38, 71, 131, maxL + 5]
+    out = torch.zeros((N, maxL), dtype=torch.uint8, device=dev)
+    first = X[:, 0].contiguous()
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        words, sizes = codec.encode_device(m, X, Ld, workspace=ws_e, pos_begin=a, pos_end=b)
+        codec.decode_device(m, words, sizes, Ld, first, workspace=ws_d, pos_begin=a, pos_end=b, out=out)
+        nm.check()
+        # the oracle coder on the whole-sequence logits of positions [a, min(b, len))
+        span = b - a
+        rows = np.zeros((N, span, 256), np.float32)
+        syms = np.zeros((N, span), np.int32)
+        counts = np.zeros(N, np.int32)
+        for i, n in enumerate(lens):
+            k = max(0, min(b, n) - a)
+            counts[i] = k
+            if k:
+                rows[i, :k] = lg[i, a - 1:a - 1 + k]
+                syms[i, :k] = host[i, a:a + k]
+        w, s, st = orc.encode(rows, syms, counts, 16, orc.MODE_BQ, pitch=words.shape[1])
+        assert st == 0
+        wh, sh = words.cpu().numpy().view(np.uint32), sizes.cpu().numpy()
+        for i in range(N):
+            if counts[i]:
+                assert sh[i] == s[i] and np.array_equal(wh[i, :sh[i]], w[i, :s[i]]), (a, b, i)
+    assert torch.equal(out.cpu(), torch.from_numpy(host))

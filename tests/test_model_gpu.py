@@ -12,7 +12,7 @@ from oracle import model_oracle as mo
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("fmt,tol", [(0, 2e-3), (1, 1.6e-2), (2, 2e-3)])   # tf32, bf16, fp16
+@pytest.mark.parametrize("fmt,tol", [(0, 2e-3), (1, 1.6e-2), (2, 2e-3), (3, 1e-5)])   # tf32, bf16, fp16, 3xTF32
 @pytest.mark.parametrize("M,K", [(128, 64), (256, 256), (512, 1024)])
 def test_diag_gemm(fmt, tol, M, K):
     rng = np.random.default_rng(M + K + fmt)
@@ -24,6 +24,11 @@ def test_diag_gemm(fmt, tol, M, K):
     ref = W.astype(np.float64) @ X.astype(np.float64).T
     err = np.abs(out - ref).max() / np.sqrt(K)
     assert err < tol, err
+    if fmt == 3:
+        # the split kind is as accurate as an fp32 GEMM on the CPU, to within a small factor
+        err32 = np.abs((W @ X.T).astype(np.float64) - ref).max() / np.sqrt(K)
+        print(f"3xTF32 M={M} K={K}: {err:.2e} (fp32 CPU GEMM {err32:.2e})")
+        assert err < 8 * err32 + 1e-7, (err, err32)
 
 
 def _native_logits(model, tokens):
@@ -37,8 +42,8 @@ def _oracle_logits(model, tokens, dtype=torch.float64):
     return mo.forward(sd, cfg, torch.from_numpy(tokens).long(), dtype=dtype).float()
 
 
-@pytest.mark.parametrize("d,L,fmt", [(64, 2, "tf32"), (64, 2, "fp16"), (256, 2, "tf32"), (256, 2, "fp16"),
-                                     (512, 1, "bf16")])
+@pytest.mark.parametrize("d,L,fmt", [(64, 2, "tf32x3"), (64, 2, "tf32"), (64, 2, "fp16"), (256, 2, "tf32"),
+                                     (256, 2, "fp16"), (512, 1, "bf16")])
 def test_logits_match_oracle(d, L, fmt):
     from model import seeded_model
     m = seeded_model(d, L, weight_format=fmt)
@@ -122,3 +127,82 @@ def test_evaluate_bpp_matches_oracle():
         n += b[:, 1:].numel()
     ref = tot / n / math.log(2.0)
     assert abs(got - ref) < 1e-4 * ref, (got, ref)
+
+
+def _config_tokens(cfg, n_chunks, n_pos, seed):
+    """n_chunks windows of n_pos bytes taken at seeded offsets from the
+    configuration's own synthetic input (the data the bench codes)."""
+    from boa_b200 import synthetic
+    if cfg == 4:
+        data = synthetic.hep_records(4 << 20, 3) + synthetic.cfd_field(256, (3, 1))[:4 << 20]
+    else:
+        data = synthetic.config_data(cfg)
+    buf = np.frombuffer(data, dtype=np.uint8)
+    rng = np.random.default_rng(seed)
+    offs = rng.integers(0, len(buf) - n_pos, n_chunks)
+    return np.stack([buf[o:o + n_pos] for o in offs]).astype(np.int64)
+
+
+def _bf16_rounded(model):
+    """The state_dict of a bf16-weight model: every projection weight rounded
+    to bf16 (configuration 4 specifies bf16 weights), the rest fp32."""
+    sd = {k: v.detach().float().cpu() for k, v in model.state_dict().items()}
+    for k in list(sd):
+        if k.endswith(".weight") and sd[k].ndim == 2 and "embedding" not in k:
+            sd[k] = sd[k].to(torch.bfloat16).float()
+    return sd
+
+
+@pytest.mark.parametrize("fmt", ["tf32x3", "tf32", "fp16"])
+def test_logits_match_oracle_config2_shape(fmt):
+    """The benchmarked model shape (d_model 256, 8 layers) on 32 chunks x 64
+    positions of the configuration-2 records: probabilities within 1e-3 of
+    the fp64 oracle for every operand kind (north_star's bound; 3xTF32 is the
+    bench's kind), and 3xTF32 within 1e-5."""
+    from model import seeded_model
+    m = seeded_model(256, 8, weight_format=fmt)
+    toks = _config_tokens(2, 32, 64, 7)
+    got = _native_logits(m, toks)
+    ref = _oracle_logits(m, toks)
+    pdiff = (torch.softmax(got, -1) - torch.softmax(ref, -1)).abs().max().item()
+    print(f"d256 L8 {fmt}: max |dp| = {pdiff:.3e}, max |dlogit| = {(got - ref).abs().max().item():.3e}")
+    assert pdiff < 1e-3
+    if fmt == "tf32x3":
+        assert pdiff < 1e-5
+
+
+def test_logits_match_oracle_config4_shape():
+    """Configuration 4's model (d_model 512, 16 layers, bf16 weights, fp32
+    accumulation and state) on 32 chunks x 64 positions of its own input,
+    against the fp64 oracle of the same bf16-weight model: within 1e-3."""
+    from model import seeded_model
+    m = seeded_model(512, 16, weight_format="bf16")
+    toks = _config_tokens(4, 32, 64, 8)
+    got = _native_logits(m, toks)
+    sd = _bf16_rounded(m)
+    ref = mo.forward(sd, mo.config_from_state_dict(sd), torch.from_numpy(toks), dtype=torch.float64).float()
+    pdiff = (torch.softmax(got, -1) - torch.softmax(ref, -1)).abs().max().item()
+    sd32 = {k: v.detach().float().cpu() for k, v in m.state_dict().items()}
+    ref32 = mo.forward(sd32, mo.config_from_state_dict(sd32), torch.from_numpy(toks), dtype=torch.float64).float()
+    pdiff32 = (torch.softmax(got, -1) - torch.softmax(ref32, -1)).abs().max().item()
+    print(f"d512 L16 bf16: max |dp| = {pdiff:.3e} vs the bf16-weight model, {pdiff32:.3e} vs fp32 weights")
+    assert pdiff < 1e-3
+
+
+def test_split_kind_identical_across_decompositions():
+    """3xTF32 at the benchmarked shape: 8-chunk single CTAs (decode of a
+    small batch), 16-chunk CTAs (>= 16 x SMs chunks) and time blocks of 4
+    positions (encode / logits) give the same bits for the same chunk."""
+    from model import seeded_model
+    m = seeded_model(256, 8, weight_format="tf32x3")
+    nm = m.native(torch.device("cuda", 0))
+    rng = np.random.default_rng(13)
+    base = rng.integers(0, 256, (20, 6)).astype(np.int64)
+    nm.set_time_block(1)
+    small = _native_logits(m, base)                                  # 8 value columns per CTA
+    big = np.concatenate([base, rng.integers(0, 256, (2400 - 20, 6))])
+    got_big = _native_logits(m, big)[:20]                            # 16 value columns per CTA
+    nm.set_time_block(4)
+    got_tb = _native_logits(m, base)                                 # 4 chunks x 4 positions per CTA
+    assert torch.equal(small, got_big)
+    assert torch.equal(small, got_tb)
