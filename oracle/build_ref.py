@@ -49,7 +49,23 @@ def module_path() -> str:
     return os.path.join(OUT_DIR, MOD_NAME + EXTENSION_SUFFIXES[0])
 
 
-def build(reference: str = "/root/reference", force: bool = False) -> str | None:
+def reference_root() -> str | None:
+    """Where the reference checkout is: $BOA_REFERENCE_ROOT, else a directory
+    named ``reference`` beside this repository's root (a sibling checkout);
+    None when neither exists (e.g. on a GPU box, which uses the prebuilt
+    module)."""
+    env = os.environ.get("BOA_REFERENCE_ROOT")
+    if env:
+        return env if os.path.isdir(env) else None
+    sib = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference")
+    return sib if os.path.isdir(sib) else None
+
+
+def build(reference: str | None = None, force: bool = False) -> str | None:
+    reference = reference or reference_root()
+    if not reference:
+        print("[build_ref] no reference checkout found ($BOA_REFERENCE_ROOT unset, no sibling 'reference'); skipping")
+        return None
     src_py = os.path.join(reference, "gpu_range_coder.py")
     if not os.path.exists(src_py):
         print(f"[build_ref] reference not present at {reference}; skipping")
@@ -97,7 +113,7 @@ def load():
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None, help="reference checkout (default: see reference_root())")
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args()
     r = build(a.reference, a.force)

@@ -17,6 +17,11 @@ Fixtures:
       oracle logits (computed in fp64, stored fp32) of that model for 3 streams x 24 seeded tokens.
   synthetic.json
       sha256 of the config-1 input and of the first 1 MiB of the config-2 input.
+  ref_weights.json
+      sha256 and size of the .bin that the reference's own weight exporter
+      (portability_solved_cpp/convert_boa_weights.py:16-135, imported from the
+      reference tree) writes for the seeded models at the configuration
+      shapes (d_model 64 / 2 layers, 256 / 8): pins boa_b200.weights.write_bin.
   bq_tables.npz
       seeded logit rows (wide, narrow, near-deterministic, NaN, +inf, K = 256
       and K = 37) and their BQ integer-quantiser CDFs at totals 2^16 and 2^24
@@ -78,14 +83,40 @@ def load_reference_boa(reference: str):
     return mod
 
 
+WEIGHT_PIN_SHAPES = [(64, 2), (256, 8)]
+
+
+def write_ref_weights(reference: str):
+    """Run the reference exporter on the seeded state_dicts; record digests."""
+    import tempfile
+    from model import seeded_model
+    spec = importlib.util.spec_from_file_location(
+        "reference_convert", os.path.join(reference, "portability_solved_cpp", "convert_boa_weights.py"))
+    conv = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(conv)
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        for d, L in WEIGHT_PIN_SHAPES:
+            pt, bn = os.path.join(tmp, "m.pt"), os.path.join(tmp, "m.bin")
+            torch.save(seeded_model(d, L).state_dict(), pt)
+            conv.convert(pt, bn)
+            raw = open(bn, "rb").read()
+            out[f"d{d}_L{L}"] = {"d_model": d, "num_layers": L, "seed": 0, "bytes": len(raw),
+                                 "sha256": hashlib.sha256(raw).hexdigest()}
+    with open(os.path.join(HERE, "ref_weights.json"), "w") as f:
+        json.dump(out, f, indent=1)
+
+
 class BoaBytePredictor(torch.nn.Module):
     """Stand-in whose class name gives the reference fingerprint."""
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None,
+                    help="reference checkout (default: $BOA_REFERENCE_ROOT or a sibling 'reference' directory)")
     ap.add_argument("--only-bq", action="store_true", help="write bq_tables.npz only (no reference tree needed)")
+    ap.add_argument("--only-weights", action="store_true", help="write ref_weights.json only")
     a = ap.parse_args()
     if a.only_bq:
         write_bq_tables()
@@ -96,7 +127,14 @@ def main():
     from oracle import model_oracle as mo
 
     # --- container written by the reference ---
-    ref = load_reference_boa(a.reference)
+    from oracle.build_ref import reference_root
+    root = a.reference or reference_root()
+    if not root:
+        raise SystemExit("make_golden: no reference checkout (pass --reference or set BOA_REFERENCE_ROOT)")
+    write_ref_weights(root)
+    if a.only_weights:
+        return
+    ref = load_reference_boa(root)
     comp, first, ulen, chunk_len, last = container_case()
     path = os.path.join(HERE, "ref_container.boa")
     bf = ref.BOA("cpu", path, BoaBytePredictor())
