@@ -13,8 +13,9 @@ Differences by design:
     GPU per rank); each rank codes its range, the per-chunk word counts and
     first bytes are all-gathered (the only collective), and every rank writes
     its own payload bytes at the offsets that the gathered counts imply.
-    ``decompress`` splits the index the same way and all-gathers the decoded
-    bytes so every rank returns the whole file.
+    ``decompress`` splits the index the same way; each rank writes its decoded
+    chunks at their offsets in a shared output file (no collective moves
+    data) and every rank returns the whole file read back from it.
 """
 from __future__ import annotations
 
@@ -26,7 +27,7 @@ import torch
 
 import codec as _codec
 from boa_b200 import container as C
-from boa_b200.shard import gather_lengths, shard_range, write_sharded
+from boa_b200.shard import gather_lengths, shard_range, write_decoded, write_sharded
 
 
 def _dist():
@@ -164,7 +165,10 @@ def BOA(device, filepath: str, model):
                 print(f"Compression complete: {n_chunks} chunks, chunk_len={chunk_len}, last={last}")
 
         # ------------------------------------------------------------------
-        def decompress(self, progress: bool = True) -> bytes:
+        def decompress(self, progress: bool = True, out_path: str | None = None) -> bytes:
+            """boa.py:274-308.  With several ranks, the decoded file is assembled
+            in `out_path` (default: this file's path + '.decoded'), each rank
+            writing its own chunks there; every rank returns the whole file."""
             self._read_file()
             bq, precision = C.flags_precision(self._flags)
             if not bq:
@@ -186,8 +190,9 @@ def BOA(device, filepath: str, model):
             mine = b"".join(parts)
             if not dist:
                 return mine
-            objs = [None] * world
-            dist.all_gather_object(objs, mine)
-            return b"".join(objs)
+            target = Path(out_path) if out_path else Path(str(self.filepath) + ".decoded")
+            write_decoded(target, int(self.metadata["uncompressed_len"]), int(self.metadata["chunk_len"]), lo, mine,
+                          dist, rank)
+            return target.read_bytes()
 
     return BoaFile(filepath, model)

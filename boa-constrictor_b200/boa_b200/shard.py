@@ -6,8 +6,11 @@ equal counts are equal bytes).  The only exchange is one all-reduce over
 disjoint per-chunk slots, which gathers every chunk's compressed byte length
 and first byte; each rank then knows every payload offset (an exclusive
 prefix sum) and writes its own payload bytes at its offset in the shared
-output file.  Rank 0 writes the header first and the index last.  There is no
-data-path collective.
+output file.  Rank 0 writes the header first and the index last.  Decompress
+needs no exchange at all: chunk i's bytes start at i * chunk_len, so each rank
+writes its decoded chunks straight into the shared output file.  No data-path
+collective; the process group carries only the length all-reduce and
+barriers.
 """
 from __future__ import annotations
 
@@ -60,3 +63,20 @@ def write_sharded(path, header: bytes, index_fn, sizes_bytes, lo: int, payload: 
     if dist is not None:
         dist.barrier()
     return offsets
+
+
+def write_decoded(path, total_len: int, chunk_len: int, lo: int, payload: bytes, dist, rank: int) -> None:
+    """Rank 0 creates `path` with total_len bytes; every rank then writes its
+    decoded chunks (which start with chunk `lo`) at byte offset
+    lo * chunk_len.  Returns once every rank has written."""
+    if rank == 0:
+        with open(path, "wb") as f:
+            f.truncate(total_len)
+    if dist is not None:
+        dist.barrier()
+    if payload:
+        with open(path, "r+b") as f:
+            f.seek(lo * chunk_len)
+            f.write(payload)
+    if dist is not None:
+        dist.barrier()

@@ -21,16 +21,20 @@ def _chunks(seed, lens):
 
 
 @need2
-@pytest.mark.parametrize("d,fmt", [(64, "tf32"), (256, "fp16")])
-def test_encode_on_gpu0_decode_on_gpu1(d, fmt):
+@pytest.mark.parametrize("d,L,fmt", [(64, 2, "tf32x3"), (256, 8, "tf32x3"), (256, 2, "fp16")])
+def test_encode_on_gpu0_decode_on_last_gpu(d, L, fmt):
+    """Configuration 3's cross-GPU round trip: encode on GPU 0, decode on the
+    box's last GPU (GPU 7 on an 8-GPU box), and re-encode there to the same
+    words."""
     import codec
     from model import seeded_model
-    m = seeded_model(d, 2, weight_format=fmt)
+    last = f"cuda:{torch.cuda.device_count() - 1}"
+    m = seeded_model(d, L, weight_format=fmt)
     xs = _chunks(21, [1, 5, 64, 200, 333] * 4)
     comp, first, Ls = codec.compress_GPU(m, xs, device="cuda:0")
-    outs = codec.decompress_GPU(m, comp, Ls, first, device="cuda:1")
+    outs = codec.decompress_GPU(m, comp, Ls, first, device=last)
     assert all(np.array_equal(x.numpy(), o) for x, o in zip(xs, outs))
-    comp1, _, _ = codec.compress_GPU(m, xs, device="cuda:1")
+    comp1, _, _ = codec.compress_GPU(m, xs, device=last)
     assert all(np.array_equal(a, b) for a, b in zip(comp, comp1))
 
 

@@ -16,7 +16,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from boa_b200 import container as C
-from boa_b200.shard import gather_lengths, shard_range, write_sharded
+from boa_b200.shard import gather_lengths, shard_range, write_decoded, write_sharded
 
 
 def _fake_words(chunk: np.ndarray) -> np.ndarray:
@@ -76,3 +76,28 @@ def test_shard_ranges_cover_all_chunks():
             got = [shard_range(n, w, r) for r in range(w)]
             assert got[0][0] == 0 and got[-1][1] == n
             assert all(got[i][1] == got[i + 1][0] for i in range(w - 1))
+
+
+def _decode_worker(rank, world, port, path, data, n_chunks):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        chunk_len, n, last = C.chunking(len(data), 0, n_chunks)
+        lo, hi = shard_range(n, world, rank)
+        mine = data[lo * chunk_len:min(hi * chunk_len, len(data))]     # this rank's "decoded" chunks
+        write_decoded(path, len(data), chunk_len, lo, mine, dist, rank)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n_chunks,world", [(5, 2), (33, 2), (7, 3)])
+def test_ranks_assemble_decoded_file_without_a_data_collective(tmp_path, n_chunks, world):
+    """Multi-rank decompress: each rank writes its own decoded chunks at
+    chunk_index * chunk_len of one shared file; only barriers are exchanged."""
+    rng = np.random.default_rng(100 + n_chunks)
+    data = rng.integers(0, 256, 3000 + n_chunks).astype(np.uint8).tobytes()
+    out = tmp_path / "dec.bin"
+    mp.start_processes(_decode_worker, args=(world, _free_port(), str(out), data, n_chunks), nprocs=world,
+                       join=True, start_method="spawn")
+    assert out.read_bytes() == data
