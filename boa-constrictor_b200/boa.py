@@ -88,8 +88,13 @@ def BOA(device, filepath: str, model):
         def get_metadata(self):
             return dict(self.metadata)
 
-        def _encode_wave(self, mm, lens, chunk_len, b0, b1):
-            """Code chunks [b0, b1): (first bytes, per-chunk little-endian u32 payloads)."""
+        # Waves are pipelined: while the kernel codes wave k, the host packs
+        # wave k + 1 into pinned memory and writes out wave k - 1.  A wave's
+        # results are read (and the model's device-side errors checked) only
+        # when it is the one wave in flight, so each error is attributed to
+        # its wave before that wave is written.
+        def _pack_wave(self, mm, lens, chunk_len, b0, b1):
+            """Chunks [b0, b1) of the input in pinned host memory (CPU work)."""
             nb = b1 - b0
             maxL = max(lens[b0:b1])
             host = torch.zeros((nb, maxL), dtype=torch.uint8, pin_memory=True)
@@ -97,12 +102,40 @@ def BOA(device, filepath: str, model):
             for j, i in enumerate(range(b0, b1)):
                 s = i * chunk_len
                 hv[j, :lens[i]] = mm[s:s + lens[i]]
+            return host, lens[b0:b1]
+
+        def _enqueue_encode(self, packed):
+            """H2D, encode kernel and D2H of one packed wave, all asynchronous."""
+            host, wl = packed
             X = host.to(dev, non_blocking=True)
-            L_d = torch.tensor(lens[b0:b1], dtype=torch.int32).to(dev, non_blocking=True)
+            L_d = torch.tensor(wl, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
             words, sizes = _codec.encode_device(self.model, X, L_d, precision=self.precision)
-            sz = sizes.cpu().numpy().astype(np.int64)
-            wh = words.cpu().numpy().view(np.uint32)
-            return hv[:, 0].astype(np.int64), [wh[j, :sz[j]].astype("<u4").tobytes() for j in range(nb)]
+            w_h = torch.empty(words.shape, dtype=words.dtype, pin_memory=True)
+            s_h = torch.empty(sizes.shape, dtype=sizes.dtype, pin_memory=True)
+            w_h.copy_(words, non_blocking=True)
+            s_h.copy_(sizes, non_blocking=True)
+            return host, w_h, s_h
+
+        def _finish_encode(self, pending):
+            """Wait for the wave in flight: (first bytes, per-chunk u32 LE payloads)."""
+            host, w_h, s_h = pending
+            self.model._native_handle(dev).check()
+            sz = s_h.numpy().astype(np.int64)
+            wh = w_h.numpy().view(np.uint32)
+            return host.numpy()[:, 0].astype(np.int64), [wh[j, :sz[j]].astype("<u4").tobytes()
+                                                         for j in range(len(sz))]
+
+        def _encode_waves(self, mm, lens, chunk_len, b_first, b_end, stream_n):
+            """Yield (first bytes, payloads) of the waves of chunks [b_first, b_end), in order."""
+            pending = None
+            for b0 in range(b_first, b_end, stream_n):
+                packed = self._pack_wave(mm, lens, chunk_len, b0, min(b0 + stream_n, b_end))
+                done = self._finish_encode(pending) if pending is not None else None
+                pending = self._enqueue_encode(packed)
+                if done is not None:
+                    yield done
+            if pending is not None:
+                yield self._finish_encode(pending)
 
         # ------------------------------------------------------------------
         def compress(self, data_path: str, seq_size: int = 0, chunks_count: int = 0, progress: bool = True,
@@ -132,9 +165,8 @@ def BOA(device, filepath: str, model):
             if dist is None:
                 w = C.StreamingWriter(self.filepath, hdr, n_chunks, resume=resume)
                 try:
-                    for b0 in range(w.chunks_done, n_chunks, stream_n):
-                        b1 = min(b0 + stream_n, n_chunks)
-                        firsts, payload = self._encode_wave(mm, lens, chunk_len, b0, b1)
+                    for firsts, payload in self._encode_waves(mm, lens, chunk_len, w.chunks_done, n_chunks,
+                                                              stream_n):
                         w.append(firsts, payload)
                     w.finish()
                 finally:
@@ -148,12 +180,13 @@ def BOA(device, filepath: str, model):
             sizes_local = np.zeros(hi - lo, dtype=np.int64)
             firsts_local = np.zeros(hi - lo, dtype=np.int64)
             payloads = []
-            for b0 in range(lo, hi, stream_n):
-                b1 = min(b0 + stream_n, hi)
-                firsts, payload = self._encode_wave(mm, lens, chunk_len, b0, b1)
+            b0 = lo
+            for firsts, payload in self._encode_waves(mm, lens, chunk_len, lo, hi, stream_n):
+                b1 = b0 + len(payload)
                 firsts_local[b0 - lo:b1 - lo] = firsts
                 sizes_local[b0 - lo:b1 - lo] = [len(x) for x in payload]
                 payloads.append(b"".join(payload))
+                b0 = b1
             sizes_bytes, firsts = gather_lengths(dist, n_chunks, lo, hi, sizes_local, firsts_local)
             write_sharded(self.filepath, hdr, lambda offs: C.index_bytes(firsts.tolist(), offs.tolist(),
                                                                          sizes_bytes.tolist()),
@@ -163,6 +196,35 @@ def BOA(device, filepath: str, model):
             self.lengths = lens
             if progress and rank == 0:
                 print(f"Compression complete: {n_chunks} chunks, chunk_len={chunk_len}, last={last}")
+
+        def _pack_words(self, lens, precision, b0, b1):
+            """The words, sizes, lengths and first bytes of chunks [b0, b1) in pinned memory."""
+            wl = lens[b0:b1]
+            comp = [np.frombuffer(c, dtype="<u4") for c in self.compressed_data[b0:b1]]
+            pitch = max(_codec.pitch_words_for(max(wl), precision), max(len(c) for c in comp))
+            words = torch.zeros((b1 - b0, pitch), dtype=torch.int32, pin_memory=True)
+            wv = words.numpy().view(np.uint32)
+            for j, c in enumerate(comp):
+                wv[j, :len(c)] = c
+            meta = torch.tensor([[len(c) for c in comp], list(wl), [int(b) & 0xFF for b in self.first_bytes[b0:b1]]],
+                                dtype=torch.int32).pin_memory()
+            return words, meta, wl
+
+        def _enqueue_decode(self, packed, precision):
+            words, meta, wl = packed
+            w_d = words.to(dev, non_blocking=True)
+            m_d = meta.to(dev, non_blocking=True)
+            out = _codec.decode_device(self.model, w_d, m_d[0], m_d[1], m_d[2].to(torch.uint8), max_len=max(wl),
+                                       precision=precision)
+            o_h = torch.empty(out.shape, dtype=torch.uint8, pin_memory=True)
+            o_h.copy_(out, non_blocking=True)
+            return words, meta, o_h, wl
+
+        def _finish_decode(self, pending):
+            words, meta, o_h, wl = pending
+            self.model._native_handle(dev).check()
+            ov = o_h.numpy()
+            return b"".join(ov[j, :wl[j]].tobytes() for j in range(len(wl)))
 
         # ------------------------------------------------------------------
         def decompress(self, progress: bool = True, out_path: str | None = None) -> bytes:
@@ -181,12 +243,15 @@ def BOA(device, filepath: str, model):
             lo, hi = shard_range(n, world, rank)
             stream_n = self._gpu_streams(max(hi - lo, 1))
             parts = []
+            pending = None
             for b0 in range(lo, hi, stream_n):
-                b1 = min(b0 + stream_n, hi)
-                comp = [np.frombuffer(c, dtype="<u4") for c in self.compressed_data[b0:b1]]
-                outs = _codec.decompress_GPU(self.model, comp, lens[b0:b1], self.first_bytes[b0:b1], device=dev,
-                                             precision=precision)
-                parts.extend(o.tobytes() for o in outs)
+                packed = self._pack_words(lens, precision, b0, min(b0 + stream_n, hi))
+                done = self._finish_decode(pending) if pending is not None else None
+                pending = self._enqueue_decode(packed, precision)
+                if done is not None:
+                    parts.append(done)
+            if pending is not None:
+                parts.append(self._finish_decode(pending))
             mine = b"".join(parts)
             if not dist:
                 return mine

@@ -187,14 +187,14 @@ def test_boafile_resume_after_interrupted_compress(tmp_path, monkeypatch):
     two = tmp_path / "two.boa"
     bf = BOA("cuda", str(two), m)
     calls = {"n": 0}
-    real = bf._encode_wave
+    real = bf._pack_wave
 
     def flaky(*a, **k):
         calls["n"] += 1
-        if calls["n"] > 2:
+        if calls["n"] > 3:
             raise KeyboardInterrupt("simulated stop")
         return real(*a, **k)
-    bf._encode_wave = flaky
+    bf._pack_wave = flaky
     with pytest.raises(KeyboardInterrupt):
         bf.compress(str(src), chunks_count=23, progress=False)
     BOA("cuda", str(two), m).compress(str(src), chunks_count=23, progress=False, resume=True)

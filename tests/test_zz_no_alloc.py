@@ -2,12 +2,13 @@
 allocating one (boa_rc_create + boa_rc_encode_step + boa_rc_finalize), through
 the C-ABI, on two calls in a row.
 
-It is for callers that cannot allocate device memory while they code, e.g. a
-host capturing its work into a CUDA graph (cudaMalloc is not allowed during
-capture) or a service that forbids allocation after start-up; its coder state
-lives in a static per-device array, shared by every call.  This file runs
-last so that a failure here leaves every other test already run; it also
-passes alone in a fresh process.
+It is for callers that cannot allocate device memory while they code: a
+plugin host or framework that owns the device memory pool and forbids
+allocation after start-up, or a real-time service that must not stall on
+cudaMalloc.  Its coder state lives in a static per-device array shared by
+every call; each call synchronises its stream to report errors.  This file
+runs last so that a failure here leaves every other test already run; it
+also passes alone in a fresh process.
 """
 import ctypes
 
