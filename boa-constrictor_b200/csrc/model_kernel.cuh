@@ -284,6 +284,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
   static_assert(VC % 8 == 0 && VC <= 32, "value columns");
   constexpr int NG = VC / 8;                             // groups of 8 value columns
   constexpr int kStagesK = S::STAGES;
+  constexpr int kProducers = kStagesK < 4 ? kStagesK : 4;   // weight-tile copy lanes of warp 0
   // Issuing a tcgen05.mma costs the issuing thread about as long as the tensor
   // core needs for it at N <= 64, so single-CTA kernels (whose GEMMs have two
   // or more M tiles) issue from two threads.  Each issuer walks the whole tile
@@ -352,8 +353,9 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::o_misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::o_misc + 4);
   int* nsteps_sh = reinterpret_cast<int*>(smem + S::o_misc + 8);
-  volatile long long* prod_it_sh = reinterpret_cast<volatile long long*>(smem + S::o_misc + 16);
   volatile uint16_t* slot_tile = reinterpret_cast<volatile uint16_t*>(smem + S::o_misc + 24);   // [kMaxStages]
+  // per ring slot: phase parity of the newest copy issued into it (0xff: none)
+  volatile uint8_t* slot_ph = reinterpret_cast<volatile uint8_t*>(smem + S::o_misc + 48);      // [kMaxStages]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -383,7 +385,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
     tc::mbar_init(xch_bar, kComputeWarps);                // the peer's compute warps
     for (int t = 0; t < S::kTileBars; ++t) tc::mbar_init(&tile_bar[t], 1);
     *abort_flag = 0;
-    *prod_it_sh = 0;
+    for (int s = 0; s < S::kMaxStages; ++s) slot_ph[s] = 0xffu;
     if constexpr (kIssuers == 2)
       for (int s = 0; s < S::kMaxStages; ++s) slot_tile[s] = 0xffffu;
     int ns = 0;
@@ -436,33 +438,36 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
 
   if (warp == 0) {
     // ============================== producer ==============================
-    if (lane == 0 && nsteps > 0) {
+    // A bulk copy issued by one thread takes about 470 SM cycles whatever its
+    // size up to 64 KB, and a thread's copies do not overlap, so one lane
+    // streaming 16 KB tiles delivers only ~35 B/clk.  kProducers lanes each
+    // own the ring slots st with st % kProducers == lane and fill them in
+    // tile order: the copies of different lanes overlap (~95 B/clk with 4).
+    if (lane < kProducers && nsteps > 0) {
       const uint64_t pol = tc::policy_evict_last();
-      long long it = 0;
-      int st = 0;
-      uint32_t ph = 0;
       bool ok = true;
 #ifdef BOA_PHASE_PROFILE
-      const bool prof = a.prof != nullptr && blockIdx.x == 0;
+      const bool prof = a.prof != nullptr && blockIdx.x == 0 && lane == 0;
 #else
       constexpr bool prof = false;
 #endif
       unsigned long long w_empty = 0;
       const uint8_t* base = a.wtiles + (long long)rank * a.tiles_per_step * kTileBytes;
-      for (int s = 0; s < nsteps && ok; ++s) {
-        const uint8_t* src = base;
-        for (int t = 0; t < a.tiles_per_step; ++t, ++it, src += kTileBytes) {
+      const long long total = (long long)nsteps * a.tiles_per_step;
+      for (long long r = 0; ok; ++r) {                     // ring rounds
+        for (int st = lane; st < kStagesK; st += kProducers) {
+          const long long g = r * kStagesK + st;           // tile index in consumption order
+          if (g >= total) { ok = false; break; }
           const long long tw = prof ? clock64() : 0;
-          if (!tc::mbar_wait(&empty[st], ph ^ 1u, abort_flag, kWaitBudget)) { ok = false; break; }
+          if (!tc::mbar_wait(&empty[st], (uint32_t)(r & 1) ^ 1u, abort_flag, kWaitBudget)) { ok = false; break; }
           if (prof) w_empty += clock64() - tw;
-          if constexpr (kIssuers == 2) slot_tile[st] = (uint16_t)it;
+          if constexpr (kIssuers == 2) slot_tile[st] = (uint16_t)g;
+          slot_ph[st] = (uint8_t)(r & 1);
           tc::mbar_arrive_expect_tx(&full[st], kTileBytes);
-          tc::bulk_g2s(ring + st * kTileBytes, src, kTileBytes, &full[st], pol);
-          if (++st == kStagesK) { st = 0; ph ^= 1u; }
+          tc::bulk_g2s(ring + st * kTileBytes, base + (g % a.tiles_per_step) * kTileBytes, kTileBytes, &full[st], pol);
         }
       }
       if (prof) a.prof[PF_PROD_WAIT_EMPTY] = w_empty;
-      *prod_it_sh = it;   // copies issued; teardown drains the unconsumed ones on abort
     }
   } else if (warp == 1 || (kIssuers == 2 && warp == kIssuer2Warp)) {
     // ============================= MMA issuers ============================
@@ -1112,13 +1117,11 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
   if (tid == 0 && *abort_flag) {
     atomicOr(a.err, RC_ERR_TIMEOUT);
     // weight copies still in flight must land before the CTA exits: the
-    // last kStagesK issued copies each own their ring slot's newest phase
-    const long long last = *prod_it_sh;
-    for (long long j = last > kStagesK ? last - kStagesK : 0; j < last; ++j) {
-      const int sj = (int)(j % kStagesK);
-      const uint32_t pj = (uint32_t)((j / kStagesK) & 1);
+    // newest copy issued into each ring slot is the only one that can be
+    for (int sj = 0; sj < kStagesK; ++sj) {
+      if (slot_ph[sj] == 0xffu) continue;
       const long long t0 = clock64();
-      while (!tc::mbar_try_wait(&full[sj], pj)) {
+      while (!tc::mbar_try_wait(&full[sj], (uint32_t)slot_ph[sj])) {
         if (clock64() - t0 > kWaitBudget) break;
       }
     }
