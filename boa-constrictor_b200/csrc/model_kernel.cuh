@@ -50,6 +50,11 @@
 #include "rc_device.cuh"
 #include "tc_sm100.cuh"
 
+// Lanes of the producer warp that issue weight-tile copies (see the producer).
+#ifndef BOA_TILE_PRODUCERS
+#define BOA_TILE_PRODUCERS 1
+#endif
+
 namespace boa {
 
 constexpr int kTileBytes = 16384;      // one A tile: 128 rows x 128 bytes
@@ -284,7 +289,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
   static_assert(VC % 8 == 0 && VC <= 32, "value columns");
   constexpr int NG = VC / 8;                             // groups of 8 value columns
   constexpr int kStagesK = S::STAGES;
-  constexpr int kProducers = kStagesK < 4 ? kStagesK : 4;   // weight-tile copy lanes of warp 0
+  constexpr int kProducers = kStagesK < BOA_TILE_PRODUCERS ? kStagesK : BOA_TILE_PRODUCERS;   // copy lanes of warp 0
   // Issuing a tcgen05.mma costs the issuing thread about as long as the tensor
   // core needs for it at N <= 64, so single-CTA kernels (whose GEMMs have two
   // or more M tiles) issue from two threads.  Each issuer walks the whole tile
@@ -440,9 +445,9 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
     // ============================== producer ==============================
     // A bulk copy issued by one thread takes about 470 SM cycles whatever its
     // size up to 64 KB, and a thread's copies do not overlap, so one lane
-    // streaming 16 KB tiles delivers only ~35 B/clk.  kProducers lanes each
-    // own the ring slots st with st % kProducers == lane and fill them in
-    // tile order: the copies of different lanes overlap (~95 B/clk with 4).
+    // streaming 16 KB tiles delivers ~35 B/clk on its own.  kProducers lanes
+    // each own the ring slots st with st % kProducers == lane and fill them in
+    // tile order, so the copies of different lanes overlap.
     if (lane < kProducers && nsteps > 0) {
       const uint64_t pol = tc::policy_evict_last();
       bool ok = true;
