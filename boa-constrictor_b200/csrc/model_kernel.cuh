@@ -446,8 +446,12 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
     // A bulk copy issued by one thread takes about 470 SM cycles whatever its
     // size up to 64 KB, and a thread's copies do not overlap, so one lane
     // streaming 16 KB tiles delivers ~35 B/clk on its own.  kProducers lanes
-    // each own the ring slots st with st % kProducers == lane and fill them in
-    // tile order, so the copies of different lanes overlap.
+    // (BOA_TILE_PRODUCERS, default 1) each own the ring slots st with
+    // st % kProducers == lane and fill them in tile order, so the copies of
+    // different lanes overlap.  Measured on config 2 the kernel does not run
+    // faster with 2 or 4 lanes, nor with 32 / 64 KB copies of 2 / 4 tiles: a
+    // slot's round trip (copy, wait, MMAs, release) with the ring's depth, not
+    // the copy rate, bounds the GEMM phases.
     if (lane < kProducers && nsteps > 0) {
       const uint64_t pol = tc::policy_evict_last();
       bool ok = true;
