@@ -317,34 +317,51 @@ def run_ours(args, cfg, rank, world, local_rank, dist):
     Ld = torch.tensor(lens, dtype=torch.int32, device=dev)
     lens_np = np.asarray(lens, np.int64)
     first = X[:, 0].contiguous()
-    ws_e = torch.empty(nm.workspace_bytes(n), dtype=torch.uint8, device=dev)
-    ws_d = torch.empty_like(ws_e)
     out = torch.zeros((n, maxL), dtype=torch.uint8, device=dev)
+    # Waves: each direction keeps its recurrent state for the chunks of one
+    # wave; waves hold as many chunks as two states fit in 60 % of the free
+    # device memory (all of them, except for configuration 4)
+    free_b, _ = torch.cuda.mem_get_info(dev)
+    per_chunk = nm.workspace_bytes(32) / 32
+    wave = int(min(n, max(32, (0.6 * free_b / (2 * per_chunk)) // 32 * 32)))
+    waves = [(w0, min(w0 + wave, n)) for w0 in range(0, n, wave)]
+    ws_e = torch.empty(nm.workspace_bytes(wave), dtype=torch.uint8, device=dev)
+    ws_d = torch.empty_like(ws_e)
     stream = torch.cuda.current_stream(dev)
     S = max(1, args.segment)
     segs = [(a, min(a + S, maxL)) for a in range(1, max(maxL, 2), S)]
     nseg = len(segs)
+    n_units = nseg * len(waves)            # one pass: every segment of every wave
+
+    def unit(k):
+        """Step k's (wave, segment): the segments of a wave in order, then the next wave."""
+        k %= n_units
+        return waves[k // nseg], segs[k % nseg]
 
     def seg_bytes(k):
-        """Input bytes a step over segment k accounts for: its coded
-        positions, plus the raw first byte of every chunk for segment 0."""
-        a, b = segs[k]
-        coded = int(np.clip(np.minimum(lens_np, b) - a, 0, None).sum())
-        return coded + (n if a == 1 else 0)
+        """Input bytes a step accounts for: its coded positions, plus the raw
+        first byte of every chunk for a wave's first segment."""
+        (w0, w1), (a, b) = unit(k)
+        coded = int(np.clip(np.minimum(lens_np[w0:w1], b) - a, 0, None).sum())
+        return coded + ((w1 - w0) if a == 1 else 0)
 
     def step(k):
-        a, b = segs[k % nseg]
-        words, sizes = codec.encode_device(model, X, Ld, workspace=ws_e, pos_begin=a, pos_end=b)
+        (w0, w1), (a, b) = unit(k)
+        words, sizes = codec.encode_device(model, X[w0:w1], Ld[w0:w1], workspace=ws_e, pos_begin=a, pos_end=b)
         e_mid = torch.cuda.Event(enable_timing=True)
         e_mid.record(stream)
-        codec.decode_device(model, words, sizes, Ld, first, workspace=ws_d, pos_begin=a, pos_end=b, out=out)
+        codec.decode_device(model, words, sizes, Ld[w0:w1], first[w0:w1], workspace=ws_d, pos_begin=a, pos_end=b,
+                            out=out[w0:w1])
         return sizes, e_mid
 
-    def verify(upto):
-        """Decoded bytes equal the input for positions < upto."""
-        mask = torch.arange(maxL, device=dev)[None, :] < torch.minimum(Ld, torch.tensor(upto, device=dev))[:, None]
-        if not torch.equal(out[mask], X[mask]):
-            raise RuntimeError("round trip mismatch")
+    def verify(steps_done):
+        """Decoded bytes equal the input wherever the steps so far decoded."""
+        for k in range(min(steps_done, n_units)):
+            (w0, w1), (a, b) = unit(k)
+            o, x = out[w0:w1, a:b], X[w0:w1, a:b]
+            mask = torch.arange(a, b, device=dev)[None, :] < Ld[w0:w1, None]
+            if not torch.equal(o[mask], x[mask]):
+                raise RuntimeError("round trip mismatch")
 
     def barrier():
         if dist is not None:
@@ -354,7 +371,7 @@ def run_ours(args, cfg, rank, world, local_rank, dist):
     for w in range(max(args.warmup, 1)):
         step(w)
     nm.check()
-    verify(segs[min(max(args.warmup, 1), nseg) - 1][1])
+    verify(max(args.warmup, 1))
 
     # timed device-resident region
     out.zero_()
@@ -372,12 +389,13 @@ def run_ours(args, cfg, rank, world, local_rank, dist):
         torch.cuda.synchronize(dev)
     barrier()
     nm.check()
-    verify(segs[min(args.steps, nseg) - 1][1] if args.steps < nseg else maxL)
+    verify(args.steps)
     t_c = sum(ev[k][0].elapsed_time(mids[k]) for k in range(args.steps)) / 1000.0
     t_d = sum(mids[k].elapsed_time(ev[k][1]) for k in range(args.steps)) / 1000.0
-    step_bytes = [seg_bytes(k % nseg) for k in range(args.steps)]
+    step_bytes = [seg_bytes(k) for k in range(args.steps)]
     bytes_timed = sum(step_bytes)
-    coded_timed = sum(b - (n if segs[k % nseg][0] == 1 else 0) for k, b in enumerate(step_bytes))
+    coded_timed = sum(b - ((unit(k)[0][1] - unit(k)[0][0]) if unit(k)[1][0] == 1 else 0)
+                      for k, b in enumerate(step_bytes))
     words_timed = sum(int(sz.to(torch.int64).sum().item()) for sz in sizes_l)
     tt = torch.tensor([t_c + t_d, t_c, t_d], dtype=torch.float64, device=dev)
     if dist is not None:
@@ -393,34 +411,41 @@ def run_ours(args, cfg, rank, world, local_rank, dist):
     # end-to-end through the public host API, from pinned host segments
     e2e = None
     if not args.no_e2e:
-        rcod = codec.RangeCodec(model, lens, arr[:, 0], device=dev)
+        del ws_e, ws_d
+        torch.cuda.empty_cache()
+        n_host = min(args.steps, n_units)
         host_segs = []
-        for k in range(min(args.steps, nseg)):
-            a, b = segs[k]
-            hseg = torch.zeros((n, b - a + 1), dtype=torch.uint8).pin_memory()
-            hseg.numpy()[:] = arr[:, a - 1:b]
+        for k in range(n_host):
+            (w0, w1), (a, b) = unit(k)
+            hseg = torch.zeros((w1 - w0, b - a + 1), dtype=torch.uint8).pin_memory()
+            hseg.numpy()[:] = arr[w0:w1, a - 1:b]
             host_segs.append(hseg)
         h2d = d2h = 0
         outs = []
+        rcod, rwave = None, None
         barrier()
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
         for k in range(args.steps):
-            a, b = segs[k % nseg]
-            w_h, s_h = rcod.encode(host_segs[k % nseg], a, b)
+            (w0, w1), (a, b) = unit(k)
+            if rwave != (w0, w1):                     # a new wave: a coder for its chunks
+                rcod = None
+                rcod, rwave = codec.RangeCodec(model, lens[w0:w1], arr[w0:w1, 0], device=dev), (w0, w1)
+            hseg = host_segs[k % n_units]
+            w_h, s_h = rcod.encode(hseg, a, b)
             o_h = rcod.decode(w_h, s_h, a, b)
-            h2d += host_segs[k % nseg].numel() + w_h.nbytes + s_h.nbytes
+            h2d += hseg.numel() + w_h.nbytes + s_h.nbytes
             d2h += w_h.nbytes + s_h.nbytes + o_h.nbytes
-            if k < nseg:
+            if k < n_units:
                 outs.append(o_h)
         torch.cuda.synchronize(dev)
         te = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
         if dist is not None:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         for k, o_h in enumerate(outs):
-            a, b = segs[k]
-            ref = arr[:, a:b].copy()
-            ref[np.arange(b - a)[None, :] >= (lens_np - a)[:, None]] = 0
+            (w0, w1), (a, b) = unit(k)
+            ref = arr[w0:w1, a:b].copy()
+            ref[np.arange(b - a)[None, :] >= (lens_np[w0:w1] - a)[:, None]] = 0
             if not np.array_equal(o_h, ref):
                 raise RuntimeError("e2e round trip mismatch")
         e2e = {"value": job_bytes / MiB / float(te.item()), "unit": "MiB/s",
@@ -471,7 +496,7 @@ def run_ours(args, cfg, rank, world, local_rank, dist):
                     "reference_path": "fp32 model, softmax, build_cdf_fast at PRECISION 24, reference range coder "
                                       "(oracle/codec_oracle.py)",
                     "gpu_path": f"{fmt} kernel, integer quantiser at PRECISION 16, whole-chunk streams"}
-    passes = args.steps / nseg
+    passes = args.steps / n_units
     line = {
         "metric": "compress+decompress round-trip throughput", "value": value, "unit": "MiB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -479,12 +504,13 @@ def run_ours(args, cfg, rank, world, local_rank, dist):
         "vs_baseline": None, "dtype": DTYPES[fmt],
         "data": "synthetic (seeded HEP-like records, random-init seeded weights)",
         "config": {"workload": cfg["name"], "chunks_per_gpu": n, "chunk_len": maxL, "bytes_per_gpu": total_bytes,
-                   "step": f"positions [a, a + {S}) of every chunk, recurrent state carried between steps; "
-                           f"{nseg} steps make one pass over the input ({passes:.2f} passes timed)",
+                   "step": f"positions [a, a + {S}) of every chunk of a wave of {wave} chunks, recurrent state "
+                           f"carried between steps; {n_units} steps make one pass over the input "
+                           f"({passes:.2f} passes timed)",
                    "weights": fmt, "precision": codec.PRECISION,
                    "parallelism": f"chunk shards x{world} ({args.scaling})",
                    "l2": "inputs larger than L2: recurrent state %d MB per side" %
-                         (sb * n // 2 // 1000000)},
+                         (sb * min(wave, n) // 2 // 1000000)},
         "compress_MiBps": job_bytes / MiB / t_c,
         "decompress_MiBps": job_bytes / MiB / t_d,
         "compress_MBps_1e6": job_bytes / 1e6 / t_c,
