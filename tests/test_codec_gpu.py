@@ -262,3 +262,37 @@ def test_position_ranges_continue_the_model_state(d, L, fmt):
             if counts[i]:
                 assert sh[i] == s[i] and np.array_equal(wh[i, :sh[i]], w[i, :s[i]]), (a, b, i)
     assert torch.equal(out.cpu(), torch.from_numpy(host))
+
+
+def test_range_codec_host_round_trip():
+    """codec.RangeCodec (the public host-buffer form of the position ranges,
+    what the bench's end-to-end leg calls): segments of host bytes in, words
+    out, words in, bytes out; every segment decodes to its input, and the
+    words equal those of encode_device over the same ranges."""
+    import codec
+    m = _model(64, 2)
+    dev = torch.device("cuda", 0)
+    lens = [1, 3, 50, 99, 100, 101, 257] * 3
+    xs = _chunks(31, lens)
+    N, maxL = len(lens), max(lens)
+    host = np.zeros((N, maxL), np.uint8)
+    for i, x in enumerate(xs):
+        host[i, :lens[i]] = x.numpy()[0]
+    rc = codec.RangeCodec(m, lens, host[:, 0], device=dev)
+    X = torch.from_numpy(host).to(dev)
+    Ld = torch.tensor(lens, dtype=torch.int32, device=dev)
+    ws = torch.empty(m.native(dev).workspace_bytes(N), dtype=torch.uint8, device=dev)
+    S = 64
+    for a in range(1, maxL, S):
+        b = min(a + S, maxL)
+        seg = torch.from_numpy(np.ascontiguousarray(host[:, a - 1:b])).pin_memory()
+        w, s = rc.encode(seg, a, b)
+        out = rc.decode(w, s, a, b)
+        ref = host[:, a:b].copy()
+        ref[np.arange(b - a)[None, :] >= (np.asarray(lens) - a)[:, None]] = 0
+        assert np.array_equal(out, ref), a
+        wd, sd = codec.encode_device(m, X, Ld, workspace=ws, pos_begin=a, pos_end=b)
+        wd, sd = wd.cpu().numpy().view(np.uint32), sd.cpu().numpy()
+        for i in range(N):
+            if min(lens[i], b) > a:
+                assert s[i] == sd[i] and np.array_equal(w[i, :s[i]], wd[i, :sd[i]]), (a, i)
