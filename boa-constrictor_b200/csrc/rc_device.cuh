@@ -228,7 +228,10 @@ __device__ __forceinline__ void bq_quantise_warp(const float (&v)[Q], int K, int
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = min(amax, __shfl_xor_sync(FULL, amax, o));
     const unsigned long long freew = (unsigned long long)(total - (uint32_t)K);
-    const unsigned long long M = (freew << 32) / W;
+    // (freew << 32) < 2^56 and W >= 2^23 (the maximum entry weighs 2^23), so
+    // the fp64 quotient is within one of the floor and udiv_f64's correction
+    // returns exactly the integer quotient
+    const unsigned long long M = udiv_f64(freew << 32, W);
     uint32_t fsum = 0;
 #pragma unroll
     for (int q = 0; q < Q; ++q) {
