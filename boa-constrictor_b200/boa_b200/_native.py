@@ -21,6 +21,7 @@ BOA_ERR_CUDA = 2
 BOA_ERR_OVERFLOW = 3
 BOA_ERR_TIMEOUT = 4
 BOA_ERR_UNSUPPORTED = 5
+BOA_ERR_RANGE = 6
 
 BOA_QUANT_REF = 0
 BOA_QUANT_BQ = 1
@@ -29,6 +30,7 @@ BOA_WEIGHTS_TF32 = 0
 BOA_WEIGHTS_BF16 = 1
 BOA_WEIGHTS_F16 = 2
 BOA_WEIGHTS_TF32X3 = 3
+BOA_WEIGHTS_F16X2 = 4
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int

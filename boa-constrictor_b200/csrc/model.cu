@@ -36,9 +36,10 @@ __global__ void __launch_bounds__(256, 1) k_diag_gemm(const uint8_t* wtiles, con
   constexpr int PER = 128 / tc::OpKind<KIND>::kElemBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kBbuf = CT * 1024 * tc::OpKind<KIND>::kElemBytes;   // B operand, K up to 1024
   uint8_t* tile = smem;                              // one A tile
-  uint8_t* bbuf = smem + kTileBytes;                 // B operand, K up to 1024 fp32
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTileBytes + CT * 4096);
+  uint8_t* bbuf = smem + kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTileBytes + kBbuf);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 5);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -59,17 +60,20 @@ __global__ void __launch_bounds__(256, 1) k_diag_gemm(const uint8_t* wtiles, con
   uint32_t ph = 0;
   for (int mt = 0; mt < n_mt; ++mt) {
     for (int ks = 0; ks < n_ks; ++ks) {
-      for (int hl = 0; hl < HL; ++hl) {
+      for (int hl = 0; hl < (HL == 1 ? 1 : 2); ++hl) {
         if (tid == 0) {
           tc::mbar_arrive_expect_tx(&bars[0], kTileBytes);
           tc::bulk_g2s(tile, wtiles + (((long long)mt * n_ks + ks) * HL + hl) * kTileBytes, kTileBytes, &bars[0],
                        tc::policy_evict_first());
           if (tc::mbar_wait(&bars[0], ph, abort_flag, kWaitBudget)) {
             tc::tc_fence_after();
-            const uint32_t a0 = tc::smem_u32(tile), b0 = tc::smem_u32(bbuf) + ks * CT * 128;
+            // kind 4: the lo' tile takes rows [2 VC, 4 VC) into columns [VC, 3 VC)
+            const uint32_t row0 = (HL == 4 && hl) ? 2 * kCT * 128 : 0, dcol = (HL == 4 && hl) ? kCT : 0;
+            const uint32_t a0 = tc::smem_u32(tile), b0 = tc::smem_u32(bbuf) + ks * CT * 128 + row0;
             for (int kk = 0; kk < 4; ++kk)
-              tc::mma<KIND>(tmem + (uint32_t)(mt * CT), tc::sdesc_sw128(a0 + kk * 32), tc::sdesc_sw128(b0 + kk * 32),
-                            tc::idesc<KIND>(128, CT), (ks > 0 || hl > 0 || kk > 0) ? 1u : 0u);
+              tc::mma<KIND>(tmem + (uint32_t)(mt * CT) + dcol, tc::sdesc_sw128(a0 + kk * 32),
+                            tc::sdesc_sw128(b0 + kk * 32), tc::idesc<KIND>(128, HL == 4 ? CT / 2 : CT),
+                            (ks > 0 || hl > 0 || kk > 0) ? 1u : 0u);
             tc::mma_commit(&bars[1]);
             tc::mbar_wait(&bars[1], ph, abort_flag, kWaitBudget);   // tile buffer reusable
           }
@@ -89,6 +93,12 @@ __global__ void __launch_bounds__(256, 1) k_diag_gemm(const uint8_t* wtiles, con
         tc::tmem_ld8_sum(ta, ta + kCT, w);
         for (int n = 0; n < 8; ++n) v[n] = w[n];
         tc::tmem_ld8_sum(ta + 8, ta + kCT + 8, w);
+        for (int n = 0; n < 8; ++n) v[8 + n] = w[n];
+      } else if constexpr (HL == 4) {
+        float w[8];
+        tc::tmem_ld8_sum_s11(ta, ta + kCT, w);
+        for (int n = 0; n < 8; ++n) v[n] = w[n];
+        tc::tmem_ld8_sum_s11(ta + 8, ta + kCT + 8, w);
         for (int n = 0; n < 8; ++n) v[8 + n] = w[n];
       } else {
         tc::tmem_ld16(ta, v);
@@ -125,13 +135,14 @@ struct MTile {
 // Append the SW128 tile images of one GEMM's M tiles, each with n_ks K slices.
 // Order: M tile by M tile, or (pairs) the K slices of M tiles 2q and 2q+1
 // interleaved -- (2q, 0), (2q+1, 0), (2q, 1), ... -- which is the order in which
-// the two MMA issuers of a single-CTA kernel take them.  The split kind
-// (kind 3) emits, for every (M tile, K slice), the tile of the weights' tf32 hi
-// halves followed by the tile of their lo halves.
+// the two MMA issuers of a single-CTA kernel take them.  The split kinds emit,
+// for every (M tile, K slice), the tile of the weights' hi halves followed by
+// the tile of their lo halves (kind 3: tf32 hi, tf32 lo; kind 4: fp16 hi,
+// fp16 residual scaled by 2^11).
 static void pack_gemm(std::vector<uint8_t>& out, const std::vector<MTile>& tiles, int n_ks, int kind, bool pairs) {
   const int eb = (kind == 0 || kind == 3) ? 4 : 2;
   const int per = 128 / eb;
-  const int hl_n = kind == 3 ? 2 : 1;
+  const int hl_n = (kind == 3 || kind == 4) ? 2 : 1;
   std::vector<std::pair<int, int>> order;   // (index into tiles, ks)
   const int n_mt = (int)tiles.size();
   for (int m0 = 0; m0 < n_mt; m0 += pairs ? 2 : 1) {
@@ -159,6 +170,11 @@ static void pack_gemm(std::vector<uint8_t>& out, const std::vector<MTile>& tiles
             const uint32_t hi = to_tf32_bits(v);
             const uint32_t b = hl == 0 ? hi : to_tf32_bits(v - bits_f32(hi));
             std::memcpy(p, &b, 4);
+          } else if (kind == 4) {
+            const __half hi = __float2half_rn(v);
+            const unsigned short h =
+                hl == 0 ? __half_as_ushort(hi) : __half_as_ushort(__float2half_rn((v - __half2float(hi)) * 2048.0f));
+            std::memcpy(p, &h, 2);
           } else if (kind == 0) {
             const uint32_t b = to_tf32_bits(v);
             std::memcpy(p, &b, 4);
@@ -298,17 +314,19 @@ int launch_step(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s) {
   a.params = m->d_params;
   a.err = m->d_err;
   const int positions = a.mode == MODE_LOGITS ? a.n_steps : a.pos1 - a.pos0;
-  switch (m->D * 4 + m->kind) {
-    case 64 * 4 + 0: return launch_step_t<64, 0>(m, a, n_chunks, s, positions);
-    case 64 * 4 + 1: return launch_step_t<64, 1>(m, a, n_chunks, s, positions);
-    case 64 * 4 + 2: return launch_step_t<64, 2>(m, a, n_chunks, s, positions);
-    case 64 * 4 + 3: return launch_step_t<64, 3>(m, a, n_chunks, s, positions);
-    case 256 * 4 + 0: return launch_step_t<256, 0>(m, a, n_chunks, s, positions);
-    case 256 * 4 + 1: return launch_step_t<256, 1>(m, a, n_chunks, s, positions);
-    case 256 * 4 + 2: return launch_step_t<256, 2>(m, a, n_chunks, s, positions);
-    case 256 * 4 + 3: return launch_step_t<256, 3>(m, a, n_chunks, s, positions);
-    case 512 * 4 + 1: return launch_step_t<512, 1>(m, a, n_chunks, s, positions);
-    case 512 * 4 + 2: return launch_step_t<512, 2>(m, a, n_chunks, s, positions);
+  switch (m->D * 8 + m->kind) {
+    case 64 * 8 + 0: return launch_step_t<64, 0>(m, a, n_chunks, s, positions);
+    case 64 * 8 + 1: return launch_step_t<64, 1>(m, a, n_chunks, s, positions);
+    case 64 * 8 + 2: return launch_step_t<64, 2>(m, a, n_chunks, s, positions);
+    case 64 * 8 + 3: return launch_step_t<64, 3>(m, a, n_chunks, s, positions);
+    case 64 * 8 + 4: return launch_step_t<64, 4>(m, a, n_chunks, s, positions);
+    case 256 * 8 + 0: return launch_step_t<256, 0>(m, a, n_chunks, s, positions);
+    case 256 * 8 + 1: return launch_step_t<256, 1>(m, a, n_chunks, s, positions);
+    case 256 * 8 + 2: return launch_step_t<256, 2>(m, a, n_chunks, s, positions);
+    case 256 * 8 + 3: return launch_step_t<256, 3>(m, a, n_chunks, s, positions);
+    case 256 * 8 + 4: return launch_step_t<256, 4>(m, a, n_chunks, s, positions);
+    case 512 * 8 + 1: return launch_step_t<512, 1>(m, a, n_chunks, s, positions);
+    case 512 * 8 + 2: return launch_step_t<512, 2>(m, a, n_chunks, s, positions);
     default: break;
   }
   return boa_fail(BOA_ERR_UNSUPPORTED, "no kernel for this d_model / weight format");
@@ -363,7 +381,7 @@ int check_range(int pos_begin, int pos_end, const char* who) {
 
 template <int KIND>
 static cudaError_t diag_launch(const uint8_t* d_t, const float* d_x, float* d_o, int M, int K, uint32_t* d_e) {
-  const int smem = kTileBytes + kCT * tc::OpKind<KIND>::kHiLo * 4096 + 64 + 1024;
+  const int smem = kTileBytes + kCT * tc::OpKind<KIND>::kHiLo * 1024 * tc::OpKind<KIND>::kElemBytes + 64 + 1024;
   cudaError_t e = cudaFuncSetAttribute(k_diag_gemm<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   k_diag_gemm<KIND><<<1, 256, smem>>>(d_t, d_x, d_o, M, K, d_e);
@@ -382,10 +400,16 @@ BOA_API int boa_model_create(boa_model** out, int d_model, int n_layers, int voc
     return boa_fail(BOA_ERR_UNSUPPORTED, "boa_model_create: d_model must be 64, 256 or 512");
   if (n_layers < 1 || n_layers > 64) return boa_fail(BOA_ERR_ARG, "boa_model_create: n_layers must be in [1, 64]");
   if (vocab < 2 || vocab > 256) return boa_fail(BOA_ERR_ARG, "boa_model_create: vocab must be in [2, 256]");
-  if (weight_format < 0 || weight_format > 3) return boa_fail(BOA_ERR_ARG, "boa_model_create: unknown weight format");
+  if (weight_format < 0 || weight_format > 4) return boa_fail(BOA_ERR_ARG, "boa_model_create: unknown weight format");
   if (!host_flat_weights) return boa_fail(BOA_ERR_ARG, "boa_model_create: null weights");
-  if (d_model == 512 && (weight_format == BOA_WEIGHTS_TF32 || weight_format == BOA_WEIGHTS_TF32X3))
+  if (d_model == 512 && (weight_format == BOA_WEIGHTS_TF32 || weight_format == BOA_WEIGHTS_TF32X3 ||
+                         weight_format == BOA_WEIGHTS_F16X2))
     return boa_fail(BOA_ERR_UNSUPPORTED, "boa_model_create: d_model 512 needs 16-bit weights (bf16 or fp16)");
+  if (weight_format == BOA_WEIGHTS_F16X2)
+    for (size_t i = 0; i < n_floats; ++i)
+      if (!(std::fabs(host_flat_weights[i]) < 65504.0f))
+        return boa_fail(BOA_ERR_RANGE, "boa_model_create: a weight outside the 2xFP16 range (|w| < 65504); "
+                                       "use BOA_WEIGHTS_TF32X3");
   BOA_CUDA(cudaSetDevice(device));
   boa_model* m = new boa_model();
   m->D = d_model; m->L = n_layers; m->V = vocab; m->kind = weight_format; m->device = device;
@@ -465,6 +489,9 @@ BOA_API int boa_model_status(boa_model* m, void* stream) {
     if (e & RC_ERR_TIMEOUT) return boa_fail(BOA_ERR_TIMEOUT, "model kernel: a bounded device wait timed out");
     if (e & RC_ERR_OVERFLOW) return boa_fail(BOA_ERR_OVERFLOW, "codec: a compressed stream exceeded its pitch");
     if (e & RC_ERR_SYMBOL) return boa_fail(BOA_ERR_ARG, "codec: symbol outside the vocabulary");
+    if (e & RC_ERR_RANGE)
+      return boa_fail(BOA_ERR_RANGE, "model kernel: an activation outside the 2xFP16 range (|v| < 65504); the "
+                                     "call's outputs are not valid, use BOA_WEIGHTS_TF32X3");
     return boa_fail(BOA_ERR_CUDA, "model kernel: unknown device error bits");
   }
   return BOA_OK;
@@ -588,7 +615,7 @@ BOA_API int boa_diag_timeout(int64_t budget_cycles, int device) {
 
 BOA_API int boa_diag_gemm(int weight_format, int M, int K, const float* h_w, const float* h_x, float* h_out,
                           int device) {
-  if (weight_format < 0 || weight_format > 3) return boa_fail(BOA_ERR_ARG, "boa_diag_gemm: bad format");
+  if (weight_format < 0 || weight_format > 4) return boa_fail(BOA_ERR_ARG, "boa_diag_gemm: bad format");
   const int per = (weight_format == 0 || weight_format == 3) ? 32 : 64;
   if (M < 128 || M % 128 || K < per || K % per || K > 1024 || M > 512)
     return boa_fail(BOA_ERR_ARG, "boa_diag_gemm: M in {128..512} step 128, K multiple of the slice, <= 1024");
@@ -611,7 +638,8 @@ BOA_API int boa_diag_gemm(int weight_format, int M, int K, const float* h_w, con
     if (weight_format == 0) e = diag_launch<0>(d_t, d_x, d_o, M, K, d_e);
     else if (weight_format == 1) e = diag_launch<1>(d_t, d_x, d_o, M, K, d_e);
     else if (weight_format == 2) e = diag_launch<2>(d_t, d_x, d_o, M, K, d_e);
-    else e = diag_launch<3>(d_t, d_x, d_o, M, K, d_e);
+    else if (weight_format == 3) e = diag_launch<3>(d_t, d_x, d_o, M, K, d_e);
+    else e = diag_launch<4>(d_t, d_x, d_o, M, K, d_e);
   }
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   uint32_t err = 0;

@@ -81,7 +81,7 @@ static inline int cdiv(int a, int b) { return (a + b - 1) / b; }
 
 // Projection tile counts per step for one CTA of a `split`-way cluster (must
 // match the kernel's consumption order; every rank streams the same count).
-// With the split operand kind every (M tile, K slice) is two tiles: hi, lo.
+// With the split operand kinds (3, 4) every (M tile, K slice) is two tiles: hi, lo.
 struct TilePlan {
   int per, kD, kE, kF, mtE, mtD, mtF;
   int split, ltE, ltD, ltF, ltV, hl;
@@ -90,7 +90,7 @@ struct TilePlan {
 static inline TilePlan make_plan(int D, int L, int kind, int split) {
   TilePlan p{};
   p.per = (kind == 0 || kind == 3) ? 32 : 64;
-  p.hl = kind == 3 ? 2 : 1;
+  p.hl = (kind == 3 || kind == 4) ? 2 : 1;
   const int E = 2 * D, F = 4 * D;
   p.kD = D / p.per; p.kE = E / p.per; p.kF = F / p.per;
   p.mtE = E / 128; p.mtD = cdiv(D, 128); p.mtF = F / 128;
@@ -156,7 +156,7 @@ __device__ __forceinline__ void cbar_sync() {   // named barrier over the 512 co
 // only when there are enough chunks to keep every SM busy.
 template <int D, int KIND>
 struct ChunkTileMax {
-  static constexpr int value = (KIND == 3 || (KIND != 0 && D <= 256)) ? 32 : 16;
+  static constexpr int value = KIND == 4 ? (D == 64 ? 64 : 32) : (KIND == 3 || (KIND != 0 && D <= 256)) ? 32 : 16;
 };
 
 // Shared-memory carve-up (dynamic smem, base rounded up to 1024 bytes).
@@ -285,7 +285,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
   constexpr int CHUNKS = VC / TB;                        // chunks per CTA (per cluster when SPLIT == 2)
   static_assert(TB == 1 || TB == 2 || TB == 4 || TB == 8, "time block");
   static_assert(TB == 1 || SPLIT == 1, "time blocks run on single CTAs");
-  static_assert(HL == 1 || SPLIT == 1, "the split operand kind runs on single CTAs");
+  static_assert(HL == 1 || SPLIT == 1, "the split operand kinds run on single CTAs");
   static_assert(VC % 8 == 0 && VC <= 32, "value columns");
   constexpr int NG = VC / 8;                             // groups of 8 value columns
   constexpr int kStagesK = S::STAGES;
@@ -482,7 +482,8 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
     // ============================= MMA issuers ============================
     const int p = warp == 1 ? 0 : 1;
     if (lane == 0 && nsteps > 0) {
-      const uint32_t id = tc::idesc<KIND>(128, CT);
+      // kind 4 multiplies each weight tile by half of the operand rows (§ OpKind<4>)
+      const uint32_t id = tc::idesc<KIND>(128, HL == 4 ? CT / 2 : CT);
       const uint64_t adesc0 = tc::sdesc_sw128(tc::smem_u32(ring));
       constexpr uint64_t kTileDesc = kTileBytes >> 4;      // descriptor start-address units (16 B)
       constexpr uint64_t kSliceDesc = (CT * 128) >> 4;
@@ -530,8 +531,9 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
       // Cluster kernels take the tiles M tile by M tile; single-CTA kernels
       // take M tiles in pairs with their K slices interleaved (the packing
       // order of their weight stream), tile (2q + h, ks) going to issuer h.
-      // With the split kind each (mt, ks) is the hi tile then the lo tile,
-      // both multiplied by the whole operand (hi and lo rows).
+      // With the split kinds each (mt, ks) is the hi tile then the lo tile:
+      // kind 3 multiplies both by the whole operand (hi and lo rows), kind 4
+      // the hi tile by rows [0, 2 VC) and the lo' tile by rows [2 VC, 4 VC).
       // tiles: also commit after every M tile (pair), so the epilogue of a
       // finished tile can start while later tiles run (in_proj -> conv, ff.0 -> GELU)
       auto gemm = [&](int n_mt, int n_ks, int col0, bool tiles, int b_off) -> bool {
@@ -544,9 +546,13 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
             for (int h = 0; h < nm; ++h) {
               const int mt = m0 + h;
 #pragma unroll
-              for (int hl = 0; hl < HL; ++hl) {
-                if (kIssuers == 1 || (mt & 1) == p)
-                  if (!tile_mma(tmem + (uint32_t)(col0 + mt * CT), bd, ks > 0 || hl > 0)) return false;
+              for (int hl = 0; hl < (HL == 1 ? 1 : 2); ++hl) {
+                if (kIssuers == 1 || (mt & 1) == p) {
+                  // kind 4: the lo' tile takes operand rows [2 VC, 4 VC) into columns [VC, 3 VC)
+                  const uint32_t dc = tmem + (uint32_t)(col0 + mt * CT + (HL == 4 && hl ? VC : 0));
+                  const uint64_t bo = (HL == 4 && hl) ? (uint64_t)((2 * VC * 128) >> 4) : 0ull;
+                  if (!tile_mma(dc, bd + bo, ks > 0 || hl > 0)) return false;
+                }
                 next_tile();
               }
             }
@@ -625,20 +631,28 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
     auto mark = [](int) {};
 #endif
     // Accumulators of eight (four) value columns starting at TMEM column
-    // `col` of this warp's lane quarter: one load, or with the split kind the
-    // sum of the hi-operand and lo-operand columns (col and col + VC).
+    // `col` of this warp's lane quarter: one load, or with the split kinds the
+    // sum of the columns col and col + VC (scaled by 2^-11 for kind 4).
     auto ldv8 = [&](uint32_t col, float (&v)[8]) {
-      if constexpr (HL == 2) tc::tmem_ld8_sum(tq + col, tq + col + VC, v);
+      if constexpr (HL == 4) tc::tmem_ld8_sum_s11(tq + col, tq + col + VC, v);
+      else if constexpr (HL == 2) tc::tmem_ld8_sum(tq + col, tq + col + VC, v);
       else tc::tmem_ld8(tq + col, v);
     };
     auto ldv4 = [&](uint32_t col, float (&v)[4]) {
-      if constexpr (HL == 2) tc::tmem_ld4_sum(tq + col, tq + col + VC, v);
+      if constexpr (HL == 4) tc::tmem_ld4_sum_s11(tq + col, tq + col + VC, v);
+      else if constexpr (HL == 2) tc::tmem_ld4_sum(tq + col, tq + col + VC, v);
       else tc::tmem_ld4(tq + col, v);
     };
     // operand buffer the next GEMM reads
     auto bnext = [&]() -> uint8_t* { return bbuf0 + (gemm_no % S::NBUF) * S::BBUF; };
-    // write one operand element of the next GEMM (this CTA's copy)
-    auto put_b = [&](uint8_t* buf, int n, int k, float v) { tc::store_operand<KIND>(buf, n, k, CT, v); };
+    // write one operand element of the next GEMM (this CTA's copy); kind 4
+    // records values its fp16 halves cannot hold (reported as RC_ERR_RANGE)
+    bool range_bad = false;
+    uint32_t amask_cur = 0;                  // this step's active value columns
+    auto put_b = [&](uint8_t* buf, int n, int k, float v) {
+      if constexpr (HL == 4) range_bad |= ((amask_cur >> n) & 1u) && !(fabsf(v) < 65504.0f);
+      tc::store_operand<KIND>(buf, n, k, CT, v);
+    };
     // SPLIT == 2: after all threads wrote this CTA's share of the next operand
     // (K slices [s0, s0 + ns), contiguous in the buffer), copy it into the
     // peer's buffer, 16 bytes per thread and store
@@ -734,7 +748,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
 #pragma unroll
         for (int i = 0; i < PLN; ++i) {
           const int f = lane + 32 * i;
-          tc::store_operand<KIND>(buf, n, f, CT, (v[i] - mean) * rstd * __ldg(w + f) + __ldg(b + f));
+          put_b(buf, n, f, (v[i] - mean) * rstd * __ldg(w + f) + __ldg(b + f));
         }
       }
     };
@@ -748,6 +762,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
       uint32_t amask = 0;
 #pragma unroll
       for (int n = 0; n < VC; ++n) amask |= (t0 + n % TB < lens_sh[n] ? 1u : 0u) << n;
+      amask_cur = amask;
       // state is read at a chunk's first column and written after its last
       // active one, for chunks that are still running in this step
       const uint32_t lmask = load_state ? (amask & kFirstCols) : 0u;
@@ -828,7 +843,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
               }
               if (row < PER) {
 #pragma unroll
-                for (int j = 0; j < 8; ++j) tc::store_operand<KIND>(buf, 8 * gi + j, row, CT, row < R ? v[j] : 0.f);
+                for (int j = 0; j < 8; ++j) put_b(buf, 8 * gi + j, row, row < R ? v[j] : 0.f);
               }
             }
           }
@@ -1002,7 +1017,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
         uint8_t* buf = bnext();
         for (int i = ct; i < VC * D; i += kComputeThreads) {
           const int n = i / D, f = i - (i / D) * D;
-          tc::store_operand<KIND>(buf, n, f, CT, hres[i]);
+          put_b(buf, n, f, hres[i]);
         }
       }
       arrive_act();
@@ -1104,6 +1119,10 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
             prev[n] = sym;
           }
         }
+      }
+      if constexpr (HL == 4) {
+        if (__any_sync(0xffffffffu, range_bad) && lane == 0) atomicOr(a.err, RC_ERR_RANGE);
+        range_bad = false;
       }
       cbar_sync();
       mark(PF_CODER);
@@ -1207,8 +1226,7 @@ int launch_step_t(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s,
     a.tiles_per_step = m->plan.per_step;
     a.tiles_per_layer = m->plan.per_layer;
     a.wtiles = m->d_tiles;
-    if constexpr (ChunkTileMax<D, KIND>::value == 32) return launch_step_ct<D, KIND, 32, 1, 4>(a, n_chunks, s);
-    else return launch_step_ct<D, KIND, 16, 1, 4>(a, n_chunks, s);
+    return launch_step_ct<D, KIND, ChunkTileMax<D, KIND>::value, 1, 4>(a, n_chunks, s);
   }
   if constexpr (D == 256 && (KIND == 1 || KIND == 2)) {
     if (m->has_split2 && 2 * cdiv(n_chunks, 16) <= m->n_sms) {
@@ -1221,8 +1239,10 @@ int launch_step_t(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s,
   a.tiles_per_step = m->plan.per_step;
   a.tiles_per_layer = m->plan.per_layer;
   a.wtiles = m->d_tiles;
-  if constexpr (HL == 2 && D == 64) {
-    return launch_step_ct<D, KIND, 32, 1>(a, n_chunks, s);
+  if constexpr (HL >= 2 && D == 64) {
+    return launch_step_ct<D, KIND, ChunkTileMax<D, KIND>::value, 1>(a, n_chunks, s);
+  } else if constexpr (HL == 4) {
+    return launch_step_ct<D, KIND, 32, 1>(a, n_chunks, s);      // 8 value columns, MMA N = 16
   } else {
     if constexpr (ChunkTileMax<D, KIND>::value == 32) {
       if (n_chunks >= (32 / HL) * m->n_sms) return launch_step_ct<D, KIND, 32, 1>(a, n_chunks, s);
@@ -1247,5 +1267,7 @@ BOA_DECLARE_LAUNCH(256, 2)
 BOA_DECLARE_LAUNCH(512, 2)
 BOA_DECLARE_LAUNCH(64, 3)
 BOA_DECLARE_LAUNCH(256, 3)
+BOA_DECLARE_LAUNCH(64, 4)
+BOA_DECLARE_LAUNCH(256, 4)
 
 }  // namespace boa

@@ -46,6 +46,7 @@ enum : uint32_t {
   RC_ERR_OVERFLOW = 1u,      // a stream needed more words than its pitch
   RC_ERR_SYMBOL = 2u,        // symbol outside [0, K)
   RC_ERR_TIMEOUT = 4u,       // a bounded device wait gave up
+  RC_ERR_RANGE = 8u,         // a model activation outside the operand kind's range (2xFP16: |v| >= 65504 or NaN)
 };
 
 __device__ __forceinline__ void rc_enc_reset(RcEnc& s) {

@@ -174,6 +174,34 @@ __device__ __forceinline__ void tmem_ld4_sum(uint32_t a0, uint32_t a1, float (&v
   for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]) + __uint_as_float(r[4 + i]);
 }
 
+// As tmem_ld8_sum / tmem_ld4_sum, with the second load scaled: a0 + 2^-11 a1
+// (one fma, a single rounding), for the kind-4 accumulators.
+__device__ __forceinline__ void tmem_ld8_sum_s11(uint32_t a0, uint32_t a1, float (&v)[8]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%16];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%17];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(a0), "r"(a1)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __fmaf_rn(__uint_as_float(r[8 + i]), 0x1p-11f, __uint_as_float(r[i]));
+}
+__device__ __forceinline__ void tmem_ld4_sum_s11(uint32_t a0, uint32_t a1, float (&v)[4]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%8];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%4,%5,%6,%7}, [%9];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(a0), "r"(a1)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __fmaf_rn(__uint_as_float(r[4 + i]), 0x1p-11f, __uint_as_float(r[i]));
+}
+
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
@@ -247,6 +275,24 @@ struct OpKind<3> {
   static constexpr uint32_t kFmt = 2;  // TF32 (hi and lo halves)
   static constexpr int kHiLo = 2;
 };
+// Kind 4 = 2xFP16 with a scaled residual (the error-corrected fp16 scheme of
+// Ootomo & Yokota, IJHPCA 2022): v = hi + 2^-11 lo', hi = rn_f16(v),
+// lo' = rn_f16((v - hi) * 2^11), 22 significant bits for |v| in [2^-14, 65504)
+// (below that the absolute error stays under 2^-35).  kHiLo = 4 operand rows
+// per value: hi in row n, lo' in row n + VC, hi again in row n + 2 VC and a
+// zero row at n + 3 VC (VC = CT / 4).  Every (M tile, K slice) streams the
+// weights' hi tile, then their lo' tile: the hi tile multiplies rows
+// [0, 2 VC) into accumulator columns [0, 2 VC) and the lo' tile multiplies
+// rows [2 VC, 4 VC) into columns [VC, 3 VC), so column n sums W_hi x_hi and
+// column n + VC sums W_hi x_lo' + W_lo' x_hi (scale 2^11); the value is
+// acc[n] + 2^-11 acc[n + VC] (columns [2 VC, 3 VC) hold W_lo' * 0 and are
+// never read).  Half the weight bytes and MMAs of kind 3.
+template <>
+struct OpKind<4> {
+  static constexpr int kElemBytes = 2;
+  static constexpr uint32_t kFmt = 0;  // F16 (hi and scaled lo' halves)
+  static constexpr int kHiLo = 4;
+};
 
 // Instruction descriptor: D fp32, A/B K-major, no negation/sparsity.
 template <int KIND>
@@ -303,7 +349,15 @@ __device__ __forceinline__ uint32_t rna_tf32(float v) {
 template <int KIND>
 __device__ __forceinline__ void store_operand(uint8_t* buf, int row, int k, int rows, float v) {
   uint8_t* p = buf + sw128_offset<KIND>(row, k, rows);
-  if constexpr (KIND == 3) {
+  if constexpr (KIND == 4) {
+    const int vc = rows / 4;
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn((v - __half2float(hi)) * 2048.0f);
+    *reinterpret_cast<unsigned short*>(p) = __half_as_ushort(hi);
+    *reinterpret_cast<unsigned short*>(buf + sw128_offset<KIND>(row + vc, k, rows)) = __half_as_ushort(lo);
+    *reinterpret_cast<unsigned short*>(buf + sw128_offset<KIND>(row + 2 * vc, k, rows)) = __half_as_ushort(hi);
+    *reinterpret_cast<unsigned short*>(buf + sw128_offset<KIND>(row + 3 * vc, k, rows)) = 0;
+  } else if constexpr (KIND == 3) {
     const uint32_t hi = rna_tf32(v);
     const uint32_t lo = rna_tf32(v - __uint_as_float(hi));
     *reinterpret_cast<uint32_t*>(p) = hi;

@@ -31,10 +31,13 @@ EXPAND = 2
 # Projection operand formats of the kernel.  "tf32x3" (the default) splits every
 # fp32 weight and activation into tf32 hi + lo halves whose products are summed
 # in fp32: the arithmetic of the reference's fp32 nn.Linear to within fp32
-# rounding.  "tf32", "fp16" and "bf16" are faster, narrower alternatives
-# ("bf16" is what the d_model-512 configuration specifies).
-WEIGHT_FORMATS = {"tf32x3": _n.BOA_WEIGHTS_TF32X3, "tf32": _n.BOA_WEIGHTS_TF32, "bf16": _n.BOA_WEIGHTS_BF16,
-                  "fp16": _n.BOA_WEIGHTS_F16}
+# rounding.  "f16x2" carries the same 22 significant bits as an fp16 hi and an
+# fp16 residual scaled by 2^11, at half the weight bytes, for activations
+# below 65504 in magnitude (larger ones are reported, BOA_ERR_RANGE).  "tf32",
+# "fp16" and "bf16" are faster, narrower alternatives ("bf16" is what the
+# d_model-512 configuration specifies).
+WEIGHT_FORMATS = {"tf32x3": _n.BOA_WEIGHTS_TF32X3, "f16x2": _n.BOA_WEIGHTS_F16X2, "tf32": _n.BOA_WEIGHTS_TF32,
+                  "bf16": _n.BOA_WEIGHTS_BF16, "fp16": _n.BOA_WEIGHTS_F16}
 DEFAULT_FORMAT = "tf32x3"
 
 

@@ -48,6 +48,7 @@ extern "C" {
 #define BOA_ERR_OVERFLOW 3   /* a compressed stream needed more words than its pitch */
 #define BOA_ERR_TIMEOUT 4    /* a bounded device-side wait gave up */
 #define BOA_ERR_UNSUPPORTED 5
+#define BOA_ERR_RANGE 6      /* a model activation outside the operand kind's range (BOA_WEIGHTS_F16X2) */
 
 /* Frequency-table quantisers. */
 #define BOA_QUANT_REF 0  /* fp32 probabilities -> reference build_cdf_fast (gpu_range_coder.py:57-79) */
@@ -60,6 +61,11 @@ extern "C" {
 #define BOA_WEIGHTS_TF32X3 3 /* fp32 weights and activations, each split into tf32 hi + lo halves whose
                                 products are summed in fp32 (3xTF32): the fp32-equivalent kind, and the
                                 one that matches the reference's fp32 nn.Linear (model.py:47-56,90-95) */
+#define BOA_WEIGHTS_F16X2 4  /* fp32 weights and activations, each split into an fp16 hi and an fp16
+                                residual scaled by 2^11 (22 significant bits, as 3xTF32) with fp32
+                                accumulation: half the weight bytes of BOA_WEIGHTS_TF32X3.  Activations
+                                must stay below 65504 in magnitude; otherwise the call reports
+                                BOA_ERR_RANGE.  d_model 64 and 256. */
 
 BOA_API const char* boa_last_error(void);
 BOA_API int boa_abi_version(void);
@@ -168,7 +174,8 @@ BOA_API int boa_model_set_time_block(boa_model* m, int positions);
 /* Wait for `stream`, then report (and clear) the device-side errors of the
  * model's calls enqueued so far: BOA_ERR_TIMEOUT, BOA_ERR_OVERFLOW (a coded
  * stream outgrew pitch_words), BOA_ERR_ARG (an encoded symbol outside the
- * vocabulary).  The error bits are one word per model, shared by the calls of
+ * vocabulary), BOA_ERR_RANGE (an activation outside a BOA_WEIGHTS_F16X2
+ * model's range; that call's outputs are not valid).  The error bits are one word per model, shared by the calls of
  * every stream; call this after the calls whose results you read.  Replaces
  * the unchecked per-launch cudaDeviceSynchronize of the reference coder
  * (gpu_range_coder.py:271,276,296,304). */

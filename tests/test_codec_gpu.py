@@ -23,7 +23,7 @@ def _chunks(seed, lens, alphabet=256):
     return [torch.from_numpy(rng.integers(0, alphabet, (1, n)).astype(np.uint8)) for n in lens]
 
 
-@pytest.mark.parametrize("fmt", ["tf32x3", "tf32", "fp16"])
+@pytest.mark.parametrize("fmt", ["tf32x3", "f16x2", "tf32", "fp16"])
 def test_roundtrip_ragged(fmt):
     import codec
     m = _model(fmt=fmt)
@@ -150,7 +150,8 @@ def test_roundtrip_d256_split_and_single():
     assert all(np.array_equal(a, b) for a, b in zip(comp, comp2[:40]))
 
 
-@pytest.mark.parametrize("d,fmt", [(64, "tf32"), (256, "fp16"), (64, "tf32x3"), (256, "tf32x3")])
+@pytest.mark.parametrize("d,fmt", [(64, "tf32"), (256, "fp16"), (64, "tf32x3"), (256, "tf32x3"), (64, "f16x2"),
+                                   (256, "f16x2")])
 def test_time_blocked_encode_matches_one_position_steps(d, fmt):
     """Encode in time blocks of 4 positions (the default) writes the same
     words as encode one position per kernel step, for lengths that end at
@@ -214,7 +215,7 @@ def test_roundtrip_d512_bf16():
     assert all(np.array_equal(x.numpy(), o) for x, o in zip(xs, outs))
 
 
-@pytest.mark.parametrize("d,L,fmt", [(64, 2, "tf32x3"), (256, 2, "tf32x3"), (256, 2, "fp16")])
+@pytest.mark.parametrize("d,L,fmt", [(64, 2, "tf32x3"), (256, 2, "tf32x3"), (256, 2, "fp16"), (256, 2, "f16x2")])
 def test_position_ranges_continue_the_model_state(d, L, fmt):
     """Coding [1, a), [a, b), [b, end) as three launches that carry the
     recurrent state in one workspace uses exactly the probabilities of one

@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 # 3xTF32: 22-bit operands, but the tensor core's fp32 accumulator does not
 # round to nearest, so its error grows with K faster than a CPU fp32 GEMM's
 # (2.0e-5 vs about 2e-6 at K = 1024): still 100x below the tf32 kind.
-@pytest.mark.parametrize("fmt,tol", [(0, 2e-3), (1, 1.6e-2), (2, 2e-3), (3, 5e-5)])   # tf32, bf16, fp16, 3xTF32
+@pytest.mark.parametrize("fmt,tol", [(0, 2e-3), (1, 1.6e-2), (2, 2e-3), (3, 5e-5), (4, 5e-5)])   # tf32, bf16, fp16, 3xTF32, 2xFP16
 @pytest.mark.parametrize("M,K", [(128, 64), (256, 256), (512, 1024)])
 def test_diag_gemm(fmt, tol, M, K):
     rng = np.random.default_rng(M + K + fmt)
@@ -27,10 +27,10 @@ def test_diag_gemm(fmt, tol, M, K):
     ref = W.astype(np.float64) @ X.astype(np.float64).T
     err = np.abs(out - ref).max() / np.sqrt(K)
     assert err < tol, err
-    if fmt == 3:
-        # the split kind is as accurate as an fp32 GEMM on the CPU, to within a small factor
+    if fmt in (3, 4):
+        # the split kinds are as accurate as an fp32 GEMM on the CPU, to within a small factor
         err32 = np.abs((W @ X.T).astype(np.float64) - ref).max() / np.sqrt(K)
-        print(f"3xTF32 M={M} K={K}: {err:.2e} (fp32 CPU GEMM {err32:.2e})")
+        print(f"{'3xTF32' if fmt == 3 else '2xFP16'} M={M} K={K}: {err:.2e} (fp32 CPU GEMM {err32:.2e})")
         assert err < 20 * err32 + 1e-6, (err, err32)
 
 
@@ -45,8 +45,8 @@ def _oracle_logits(model, tokens, dtype=torch.float64):
     return mo.forward(sd, cfg, torch.from_numpy(tokens).long(), dtype=dtype).float()
 
 
-@pytest.mark.parametrize("d,L,fmt", [(64, 2, "tf32x3"), (64, 2, "tf32"), (64, 2, "fp16"), (256, 2, "tf32"),
-                                     (256, 2, "fp16"), (512, 1, "bf16")])
+@pytest.mark.parametrize("d,L,fmt", [(64, 2, "tf32x3"), (64, 2, "f16x2"), (64, 2, "tf32"), (64, 2, "fp16"),
+                                     (256, 2, "tf32"), (256, 2, "fp16"), (512, 1, "bf16")])
 def test_logits_match_oracle(d, L, fmt):
     from model import seeded_model
     m = seeded_model(d, L, weight_format=fmt)
@@ -156,7 +156,7 @@ def _bf16_rounded(model):
     return sd
 
 
-@pytest.mark.parametrize("fmt", ["tf32x3", "tf32", "fp16"])
+@pytest.mark.parametrize("fmt", ["tf32x3", "f16x2", "tf32", "fp16"])
 def test_logits_match_oracle_config2_shape(fmt):
     """The benchmarked model shape (d_model 256, 8 layers) on 32 chunks x 64
     positions of the configuration-2 records: probabilities within 1e-3 of
@@ -170,7 +170,7 @@ def test_logits_match_oracle_config2_shape(fmt):
     pdiff = (torch.softmax(got, -1) - torch.softmax(ref, -1)).abs().max().item()
     print(f"d256 L8 {fmt}: max |dp| = {pdiff:.3e}, max |dlogit| = {(got - ref).abs().max().item():.3e}")
     assert pdiff < 1e-3
-    if fmt == "tf32x3":
+    if fmt in ("tf32x3", "f16x2"):
         assert pdiff < 1e-5
 
 
@@ -192,12 +192,14 @@ def test_logits_match_oracle_config4_shape():
     assert pdiff < 1e-3
 
 
-def test_split_kind_identical_across_decompositions():
-    """3xTF32 at the benchmarked shape: 8-chunk single CTAs (decode of a
-    small batch), 16-chunk CTAs (>= 16 x SMs chunks) and time blocks of 4
-    positions (encode / logits) give the same bits for the same chunk."""
+@pytest.mark.parametrize("fmt", ["tf32x3", "f16x2"])
+def test_split_kind_identical_across_decompositions(fmt):
+    """The split kinds at the benchmarked shape: one-position single CTAs
+    (8 chunks; 16 for 3xTF32 once there are >= 16 x SMs chunks) and time
+    blocks of 4 positions (encode / logits) give the same bits for the same
+    chunk."""
     from model import seeded_model
-    m = seeded_model(256, 8, weight_format="tf32x3")
+    m = seeded_model(256, 8, weight_format=fmt)
     nm = m.native(torch.device("cuda", 0))
     rng = np.random.default_rng(13)
     base = rng.integers(0, 256, (20, 6)).astype(np.int64)
@@ -209,3 +211,22 @@ def test_split_kind_identical_across_decompositions():
     got_tb = _native_logits(m, base)                                 # 4 chunks x 4 positions per CTA
     assert torch.equal(small, got_big)
     assert torch.equal(small, got_tb)
+
+
+def test_f16x2_reports_activations_out_of_range():
+    """2xFP16 holds activations below 65504 in magnitude; a model whose
+    LayerNorm output exceeds that reports BOA_ERR_RANGE at the status call
+    instead of silently coding with infinities.  The context stays usable."""
+    from model import seeded_model
+    m = seeded_model(64, 2, weight_format="f16x2")
+    with torch.no_grad():
+        m.blocks[0].ln1.weight.mul_(1e6)
+    dev = torch.device("cuda", 0)
+    toks = torch.randint(0, 256, (5, 9), device=dev)
+    m(toks)
+    with pytest.raises(_n.BoaError) as ei:
+        m.native(dev).check()
+    assert ei.value.code == _n.BOA_ERR_RANGE
+    m2 = seeded_model(64, 2, weight_format="f16x2")
+    m2(toks)
+    m2.native(dev).check()
