@@ -75,7 +75,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--weights", default=None, choices=["tf32x3", "tf32", "fp16", "bf16"])
+    ap.add_argument("--weights", default=None, choices=["tf32x3", "f16x2", "tf32", "fp16", "bf16"])
     ap.add_argument("--segment", type=int, default=4096, help="positions of every chunk coded per step")
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     ap.add_argument("--size", type=int, default=None, help="override input bytes (testing)")
@@ -289,6 +289,7 @@ def run_reference(args, cfg, rank):
 
 
 DTYPES = {"tf32x3": "f32 (3xTF32: tf32 hi + lo operand halves, fp32 accumulation)",
+          "f16x2": "f32 (2xFP16: fp16 hi + 2^11-scaled fp16 residual, 22-bit operands, fp32 accumulation)",
           "tf32": "tf32 products / f32", "fp16": "fp16 products / f32", "bf16": "bf16 products / f32"}
 
 
@@ -478,7 +479,7 @@ def run_ours(args, cfg, rank, world, local_rank, dist):
               "per_unit": f"{sb // tb} B recurrent-state read+write per coded byte"}
     # tensor pipe: the model's projection FLOPs, and what the split kind issues
     macs = gemm_macs_per_byte(cfg["d"], cfg["L"])
-    products = 4 if fmt == "tf32x3" else 1
+    products = {"tf32x3": 4, "f16x2": 3}.get(fmt, 1)
     tf_peak, tf_src = measured_tensor_peak(fmt)
     fl_d = 2.0 * macs * coded_timed * products / t_d / 1e12
     roof_t = {"bound": "tensor", "kernel": "k_boa_step decode launch, projections",

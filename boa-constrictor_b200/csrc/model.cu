@@ -32,7 +32,8 @@ template <int KIND>
 __global__ void __launch_bounds__(256, 1) k_diag_gemm(const uint8_t* wtiles, const float* X, float* out, int M, int K,
                                                       uint32_t* err) {
   constexpr int HL = tc::OpKind<KIND>::kHiLo;
-  constexpr int CT = kCT * HL;                       // operand rows (MMA N)
+  constexpr int CT = kCT * HL;                       // operand rows
+  constexpr int kTilesPer = HL == 1 ? 1 : 2;         // weight tiles per (M tile, K slice)
   constexpr int PER = 128 / tc::OpKind<KIND>::kElemBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -60,11 +61,11 @@ __global__ void __launch_bounds__(256, 1) k_diag_gemm(const uint8_t* wtiles, con
   uint32_t ph = 0;
   for (int mt = 0; mt < n_mt; ++mt) {
     for (int ks = 0; ks < n_ks; ++ks) {
-      for (int hl = 0; hl < (HL == 1 ? 1 : 2); ++hl) {
+      for (int hl = 0; hl < kTilesPer; ++hl) {
         if (tid == 0) {
           tc::mbar_arrive_expect_tx(&bars[0], kTileBytes);
-          tc::bulk_g2s(tile, wtiles + (((long long)mt * n_ks + ks) * HL + hl) * kTileBytes, kTileBytes, &bars[0],
-                       tc::policy_evict_first());
+          tc::bulk_g2s(tile, wtiles + (((long long)mt * n_ks + ks) * kTilesPer + hl) * kTileBytes, kTileBytes,
+                       &bars[0], tc::policy_evict_first());
           if (tc::mbar_wait(&bars[0], ph, abort_flag, kWaitBudget)) {
             tc::tc_fence_after();
             // kind 4: the lo' tile takes rows [2 VC, 4 VC) into columns [VC, 3 VC)
