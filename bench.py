@@ -7,9 +7,12 @@
 Default workload: configuration 2 of the benchmark spec -- 64 MiB of seeded
 HEP-like event records, chunks_count = 1000 (67,109 B per chunk), the
 BoaConstrictor d_model 256 / 8 layers model with seeded random init, and
-projections in the fp32-equivalent 3xTF32 operand kind (every fp32 weight and
-activation split into tf32 hi + lo halves, products summed in fp32; the
-reference model is fp32 nn.Linear).  Recurrent state, element-wise math and
+projections in the fp32-equivalent 2xFP16 operand kind (every fp32 weight and
+activation carried as an fp16 hi and a 2^11-scaled fp16 residual, 22
+significant bits, products accumulated in fp32; the reference model is fp32
+nn.Linear, and at this shape the kernel's probabilities are within 1.5e-8 of
+an fp64 evaluation, the reference's fp32 arithmetic within 6e-9).  --weights
+tf32x3 runs the 3xTF32 split instead.  Recurrent state, element-wise math and
 accumulation are fp32.
 
 A step is one pass of the hot path over one batch: compress, then
@@ -56,11 +59,11 @@ MiB = 1 << 20
 
 CONFIGS = {
     1: dict(name="config1 markov 1 MiB, chunks_count=16, d_model=64, num_layers=2", d=64, L=2, chunks=16,
-            data=("markov", 1 << 20), fmt="tf32x3"),
+            data=("markov", 1 << 20), fmt="f16x2"),
     2: dict(name="config2 hep-records 64 MiB, chunks_count=1000, d_model=256, num_layers=8", d=256, L=8,
-            chunks=1000, data=("hep", 64 * MiB), fmt="tf32x3"),
+            chunks=1000, data=("hep", 64 * MiB), fmt="f16x2"),
     3: dict(name="config3 hep-records 64 MiB, chunks_count=8192, d_model=256, num_layers=8", d=256, L=8,
-            chunks=8192, data=("hep", 64 * MiB), fmt="tf32x3"),
+            chunks=8192, data=("hep", 64 * MiB), fmt="f16x2"),
     4: dict(name="config4 records + CFD field 1 GiB, chunks_count=65536, d_model=512, num_layers=16, bf16",
             d=512, L=16, chunks=65536, data=("mixed", 1 << 30), fmt="bf16"),
     5: dict(name="config5 range coder only, 16384 streams x 65536 symbols, logits N(0, 3^2), BQ 2^16",
@@ -479,7 +482,7 @@ def run_ours(args, cfg, rank, world, local_rank, dist):
               "per_unit": f"{sb // tb} B recurrent-state read+write per coded byte"}
     # tensor pipe: the model's projection FLOPs, and what the split kind issues
     macs = gemm_macs_per_byte(cfg["d"], cfg["L"])
-    products = {"tf32x3": 4, "f16x2": 3}.get(fmt, 1)
+    products = {"tf32x3": 4, "f16x2": 4}.get(fmt, 1)   # tensor products issued per multiply
     tf_peak, tf_src = measured_tensor_peak(fmt)
     fl_d = 2.0 * macs * coded_timed * products / t_d / 1e12
     roof_t = {"bound": "tensor", "kernel": "k_boa_step decode launch, projections",

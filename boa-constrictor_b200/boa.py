@@ -7,7 +7,8 @@ container (boa.py:47-157).
 Differences by design:
   * every wave of chunks goes through the fused sm_100a codec kernel
     (codec.encode_device / decode_device) instead of a per-byte Python loop;
-  * ``flags`` records the quantiser (bit 0) and table precision (bits 8-15);
+  * ``flags`` records the quantiser (bit 0), the table precision (bits 8-15)
+    and the model's operand kind (bits 16-23, checked on decompress);
   * when ``torch.distributed`` is initialised with more than one rank, the
     chunks are split into contiguous, byte-balanced ranges, one per rank (one
     GPU per rank); each rank codes its range, the per-chunk word counts and
@@ -160,7 +161,8 @@ def BOA(device, filepath: str, model):
             lo, hi = shard_range(n_chunks, world, rank)
             mm = np.memmap(p, dtype=np.uint8, mode="r")
             stream_n = self._gpu_streams(max(hi - lo, 1))
-            hdr = C.header_bytes(C.make_flags(self.precision), total, chunk_len, n_chunks, last,
+            hdr = C.header_bytes(C.make_flags(self.precision, getattr(self.model, "weight_format", None)), total,
+                                 chunk_len, n_chunks, last,
                                  self._model_fingerprint())
             if dist is None:
                 w = C.StreamingWriter(self.filepath, hdr, n_chunks, resume=resume)
@@ -233,6 +235,11 @@ def BOA(device, filepath: str, model):
             writing its own chunks there; every rank returns the whole file."""
             self._read_file()
             bq, precision = C.flags_precision(self._flags)
+            wf = C.flags_weight_format(self._flags)
+            mine = getattr(self.model, "weight_format", None)
+            if wf is not None and mine is not None and wf != mine:
+                raise ValueError(f"this file was coded with {wf} projections; the model computes {mine}, whose "
+                                 f"probabilities differ: construct it with weight_format={wf!r}")
             if not bq:
                 raise ValueError("this file was coded with the reference float quantiser (flags bit 0 clear); "
                                  "its probabilities come from other kernels and cannot be reproduced bit for bit")

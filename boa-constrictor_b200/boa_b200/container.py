@@ -9,8 +9,8 @@ Layout, all little-endian::
             n x uvarint(byte lengths) | u32 crc32(index)
 
 ``flags`` is ignored by the reference reader (boa.py:121).  This build sets
-bit 0 for streams coded with its integer quantiser and stores the table
-precision in bits 8-15; files with bit 0 clear were coded with the
+bit 0 for streams coded with its integer quantiser, stores the table
+precision in bits 8-15 and the model's operand kind in bits 16-23; files with bit 0 clear were coded with the
 reference's float quantiser at precision 24.
 """
 from __future__ import annotations
@@ -28,8 +28,25 @@ FLAG_BQ = 0x1
 HEADER_FIXED = 4 + 4 + 4 + 8 + 4 + 4 + 4 + 1
 
 
-def make_flags(precision: int) -> int:
-    return FLAG_BQ | ((int(precision) & 0xFF) << 8)
+# bits 16-23 of flags: the model's projection operand kind (0: not recorded).
+# Streams decode only under the kind that coded them.
+WEIGHT_FORMAT_CODES = {"tf32": 1, "bf16": 2, "fp16": 3, "tf32x3": 4, "f16x2": 5}
+
+
+def make_flags(precision: int, weight_format: str | None = None) -> int:
+    f = FLAG_BQ | ((int(precision) & 0xFF) << 8)
+    if weight_format is not None:
+        f |= WEIGHT_FORMAT_CODES[weight_format] << 16
+    return f
+
+
+def flags_weight_format(flags: int) -> str | None:
+    """The operand kind recorded in flags, or None for files that do not record one."""
+    code = (flags >> 16) & 0xFF
+    for k, v in WEIGHT_FORMAT_CODES.items():
+        if v == code:
+            return k
+    return None
 
 
 def flags_precision(flags: int) -> tuple[bool, int]:

@@ -38,7 +38,15 @@ EXPAND = 2
 # d_model-512 configuration specifies).
 WEIGHT_FORMATS = {"tf32x3": _n.BOA_WEIGHTS_TF32X3, "f16x2": _n.BOA_WEIGHTS_F16X2, "tf32": _n.BOA_WEIGHTS_TF32,
                   "bf16": _n.BOA_WEIGHTS_BF16, "fp16": _n.BOA_WEIGHTS_F16}
-DEFAULT_FORMAT = "tf32x3"
+
+
+def default_format(d_model: int) -> str:
+    """The operand kind used when none is given: "f16x2" (fp32-equivalent; its
+    probabilities at d_model 256 / 8 layers are within 1.5e-8 of an fp64
+    evaluation, the reference's own fp32 arithmetic within 6e-9) for
+    d_model <= 256, and "bf16" for d_model 512, where the split kinds do not
+    fit shared memory and TMEM (the d_model-512 configuration specifies bf16)."""
+    return "f16x2" if d_model <= 256 else "bf16"
 
 
 class Mamba(nn.Module):
@@ -141,7 +149,7 @@ class NativeModel:
 class BoaBytePredictor(nn.Module):
     """Mamba model predicting the next byte (model.py:83-131)."""
 
-    def __init__(self, d_model=256, num_layers=4, vocab_size=256, weight_format: str = DEFAULT_FORMAT):
+    def __init__(self, d_model=256, num_layers=4, vocab_size=256, weight_format: str | None = None):
         super().__init__()
         self.embedding = nn.Embedding(vocab_size, d_model)
         self.blocks = nn.ModuleList([MambaBlock(d_model) for _ in range(num_layers)])
@@ -149,7 +157,9 @@ class BoaBytePredictor(nn.Module):
         self.d_model = d_model
         self.num_layers = num_layers
         self.vocab_size = vocab_size
-        self.weight_format = weight_format
+        self.weight_format = weight_format or default_format(d_model)
+        if self.weight_format not in WEIGHT_FORMATS:
+            raise ValueError(f"unknown weight_format {weight_format!r}; one of {sorted(WEIGHT_FORMATS)}")
         self._native = {}
 
     # -- native handle management ---------------------------------------------
@@ -215,7 +225,7 @@ class BoaBytePredictor(nn.Module):
         return out
 
 
-def BoaConstrictor(d_model=256, num_layers=4, vocab_size=256, device="cuda", weight_format: str = DEFAULT_FORMAT):
+def BoaConstrictor(d_model=256, num_layers=4, vocab_size=256, device="cuda", weight_format: str | None = None):
     """Construct a BoaBytePredictor (model.py:5-134).  Parameters are created on
     the CPU with the module-construction order of the reference (embedding,
     blocks, head) so a given torch seed always yields the same weights; the
@@ -231,7 +241,7 @@ def BoaConstrictor(d_model=256, num_layers=4, vocab_size=256, device="cuda", wei
 
 
 def seeded_model(d_model: int, num_layers: int, vocab_size: int = 256, seed: int = 0,
-                 weight_format: str = DEFAULT_FORMAT) -> BoaBytePredictor:
+                 weight_format: str | None = None) -> BoaBytePredictor:
     """The benchmark/test model: torch.manual_seed(seed) then construction."""
     torch.manual_seed(seed)
     return BoaConstrictor(d_model=d_model, num_layers=num_layers, vocab_size=vocab_size, device="cpu",

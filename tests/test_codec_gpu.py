@@ -297,3 +297,21 @@ def test_range_codec_host_round_trip():
         for i in range(N):
             if min(lens[i], b) > a:
                 assert s[i] == sd[i] and np.array_equal(w[i, :s[i]], wd[i, :sd[i]]), (a, i)
+
+
+def test_decompress_refuses_another_operand_kind(tmp_path):
+    """The file records the operand kind that coded it (flags bits 16-23);
+    decompressing with a model of another kind, whose probabilities differ,
+    is a ValueError instead of garbage."""
+    from boa import BOA
+    from boa_b200 import container as C
+    from boa_b200 import synthetic
+    data = synthetic.config_data(1)[:8192]
+    src = tmp_path / "in.bin"
+    src.write_bytes(data)
+    out = tmp_path / "o.boa"
+    BOA("cuda", str(out), _model(64, 2, "f16x2")).compress(str(src), chunks_count=4, progress=False)
+    assert C.flags_weight_format(C.parse(out.read_bytes()).flags) == "f16x2"
+    assert BOA("cuda", str(out), _model(64, 2, "f16x2")).decompress(progress=False) == data
+    with pytest.raises(ValueError, match="f16x2"):
+        BOA("cuda", str(out), _model(64, 2, "tf32x3")).decompress(progress=False)

@@ -55,6 +55,10 @@ def test_reader_matches_reference_parse():
 def test_flags_roundtrip():
     assert C.flags_precision(C.make_flags(16)) == (True, 16)
     assert C.flags_precision(0) == (False, 24)
+    for wf in C.WEIGHT_FORMAT_CODES:
+        f = C.make_flags(16, wf)
+        assert C.flags_weight_format(f) == wf and C.flags_precision(f) == (True, 16)
+    assert C.flags_weight_format(C.make_flags(16)) is None
 
 
 def test_uvarint():
