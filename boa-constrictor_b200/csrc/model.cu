@@ -460,8 +460,8 @@ BOA_API size_t boa_model_workspace_bytes(const boa_model* m, int n_chunks) {
 }
 
 BOA_API int boa_model_set_time_block(boa_model* m, int positions) {
-  if (!m || (positions != 1 && positions != 4))
-    return boa_fail(BOA_ERR_ARG, "boa_model_set_time_block: positions must be 1 or 4");
+  if (!m || (positions != 0 && positions != 1 && positions != 4 && positions != 8))
+    return boa_fail(BOA_ERR_ARG, "boa_model_set_time_block: positions must be 0, 1, 4 or 8");
   m->time_block = positions;
   return BOA_OK;
 }

@@ -51,8 +51,9 @@
 #include "tc_sm100.cuh"
 
 // Lanes of the producer warp that issue weight-tile copies (see the producer).
+// 0 (the default) picks them per kernel; a positive value forces that count.
 #ifndef BOA_TILE_PRODUCERS
-#define BOA_TILE_PRODUCERS 1
+#define BOA_TILE_PRODUCERS 0
 #endif
 
 namespace boa {
@@ -289,7 +290,10 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
   static_assert(VC % 8 == 0 && VC <= 32, "value columns");
   constexpr int NG = VC / 8;                             // groups of 8 value columns
   constexpr int kStagesK = S::STAGES;
-  constexpr int kProducers = kStagesK < BOA_TILE_PRODUCERS ? kStagesK : BOA_TILE_PRODUCERS;   // copy lanes of warp 0
+  // copy lanes of warp 0: two where measured faster (2xFP16 encode and decode,
+  // 3xTF32 decode), else one
+  constexpr int kProdWant = BOA_TILE_PRODUCERS > 0 ? BOA_TILE_PRODUCERS : ((KIND == 4 || (KIND == 3 && TB == 1)) ? 2 : 1);
+  constexpr int kProducers = kStagesK < kProdWant ? kStagesK : kProdWant;
   // Issuing a tcgen05.mma costs the issuing thread about as long as the tensor
   // core needs for it at N <= 64, so single-CTA kernels (whose GEMMs have two
   // or more M tiles) issue from two threads.  Each issuer walks the whole tile
@@ -446,12 +450,13 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
     // A bulk copy issued by one thread takes about 470 SM cycles whatever its
     // size up to 64 KB, and a thread's copies do not overlap, so one lane
     // streaming 16 KB tiles delivers ~35 B/clk on its own.  kProducers lanes
-    // (BOA_TILE_PRODUCERS, default 1) each own the ring slots st with
-    // st % kProducers == lane and fill them in tile order, so the copies of
-    // different lanes overlap.  Measured on config 2 the kernel does not run
-    // faster with 2 or 4 lanes, nor with 32 / 64 KB copies of 2 / 4 tiles: a
-    // slot's round trip (copy, wait, MMAs, release) with the ring's depth, not
-    // the copy rate, bounds the GEMM phases.
+    // each own the ring slots st with st % kProducers == lane and fill them in
+    // tile order, so the copies of different lanes overlap.  Measured at
+    // d_model 256 / 8 layers and 1000 chunks: two lanes shorten 2xFP16 encode
+    // and decode steps by about 5 % and 3xTF32 decode steps by 9 %, but
+    // lengthen 3xTF32 encode steps by 13 % and leave fp16 unchanged; three
+    // lanes are slower than two, and 32 / 64 KB copies of 2 / 4 tiles gain
+    // nothing.
     if (lane < kProducers && nsteps > 0) {
       const uint64_t pol = tc::policy_evict_last();
       bool ok = true;
@@ -1177,7 +1182,7 @@ struct boa_model {
   float* d_params = nullptr;
   uint32_t* d_err = nullptr;      // device-side error bits of the calls on this model
   size_t params_floats = 0;
-  int time_block = 4;             // positions per step in encode / logits mode (1 or 4)
+  int time_block = 0;             // positions per step in encode / logits mode: 0 (choose 4 or 8), 1, 4 or 8
 };
 
 namespace boa {
@@ -1210,10 +1215,35 @@ int launch_step_ct(StepArgs& a, int n_chunks, cudaStream_t s) {
   return BOA_OK;
 }
 
+// Time blocks of 8 positions need chunk runs of whole blocks in the scan.
+template <int D, int KIND>
+constexpr bool time_block8_ok() {
+  constexpr int VC = ChunkTileMax<D, KIND>::value / tc::OpKind<KIND>::kHiLo;
+  constexpr int LT_E = 2 * D / 128;
+  return (VC / (LT_E >= 4 ? 1 : 4 / LT_E)) % 8 == 0;
+}
+
+// Time block of an encode / logits run when the model leaves the choice open:
+// 8 when the launch then takes less time than with 4, estimated as (waves of
+// CTAs, one per SM) x (kernel steps + a CTA's start-up, about 6 steps).  Both
+// cost about the same per step, but 8 halves the steps and doubles the CTAs,
+// which fills the last wave better (1000 chunks of 2xFP16 at d_model 256:
+// 7 waves x 512 steps instead of 4 x 1024 per 4096 positions; encode about
+// 17 % faster) and halves the steps of one-wave launches.
+inline int choose_time_block(int n_chunks, int chunks_per_cta_tb1, int positions, int n_sms) {
+  constexpr int kStartSteps = 6;
+  const auto cost = [&](int tb) {
+    const long long ctas = cdiv(n_chunks, chunks_per_cta_tb1 / tb);
+    return (long long)cdiv((int)ctas, n_sms) * (cdiv(positions, tb) + kStartSteps);
+  };
+  return positions >= 8 && cost(8) < cost(4) ? 8 : 4;
+}
+
 // Pick the decomposition.  Encode and logits runs of at least 4 positions use
-// time blocks of 4 positions on the widest single-CTA tile (32 operand columns:
-// 8 chunks with 16-bit operands at d_model <= 256, 4 chunks with the split
-// kind, else 16 columns = 4 chunks).  Decode, and single steps, use one
+// time blocks of 4 or 8 positions (choose_time_block, or the model's setting)
+// on the widest single-CTA tile (32 operand columns: 8 chunks with 16-bit
+// operands at d_model <= 256, 8 value columns with 2xFP16, 16 with 3xTF32,
+// else 16 columns).  Decode, and single steps, use one
 // position per step: clusters of two CTAs (half the features each) when
 // 16-chunk tiles would leave SMs idle, 32-column tiles when there are chunks
 // enough to fill every SM, 16-column single CTAs otherwise (the split kind at
@@ -1222,11 +1252,17 @@ int launch_step_ct(StepArgs& a, int n_chunks, cudaStream_t s) {
 template <int D, int KIND>
 int launch_step_t(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s, int positions) {
   constexpr int HL = tc::OpKind<KIND>::kHiLo;
-  if (m->time_block == 4 && positions >= 4 && (a.mode == MODE_ENCODE || a.mode == MODE_LOGITS)) {
+  if (m->time_block != 1 && positions >= 4 && (a.mode == MODE_ENCODE || a.mode == MODE_LOGITS)) {
     a.tiles_per_step = m->plan.per_step;
     a.tiles_per_layer = m->plan.per_layer;
     a.wtiles = m->d_tiles;
-    return launch_step_ct<D, KIND, ChunkTileMax<D, KIND>::value, 1, 4>(a, n_chunks, s);
+    constexpr int CTM = ChunkTileMax<D, KIND>::value;
+    if constexpr (time_block8_ok<D, KIND>()) {
+      const int tb = m->time_block == 0 ? choose_time_block(n_chunks, CTM / HL, positions, m->n_sms)
+                                        : (m->time_block == 8 && positions >= 8 ? 8 : 4);
+      if (tb == 8) return launch_step_ct<D, KIND, CTM, 1, 8>(a, n_chunks, s);
+    }
+    return launch_step_ct<D, KIND, CTM, 1, 4>(a, n_chunks, s);
   }
   if constexpr (D == 256 && (KIND == 1 || KIND == 2)) {
     if (m->has_split2 && 2 * cdiv(n_chunks, 16) <= m->n_sms) {

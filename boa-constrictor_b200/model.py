@@ -117,7 +117,8 @@ class NativeModel:
         return int(_n.load().boa_model_workspace_bytes(self.h, int(n)))
 
     def set_time_block(self, positions: int) -> None:
-        """Positions per kernel step for encode / logits runs: 4 (default) or 1."""
+        """Positions per kernel step for encode / logits runs: 0 (default: each
+        launch chooses 4 or 8), 1, 4 or 8.  The output bits are the same."""
         _n.call("boa_model_set_time_block", self.h, int(positions))
 
     def check(self, stream=None) -> None:

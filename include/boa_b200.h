@@ -165,10 +165,14 @@ BOA_API int boa_model_info(const boa_model* m, int* d_model, int* n_layers, int*
  * boa_codec_* / boa_model_logits call over n_chunks streams needs. */
 BOA_API size_t boa_model_workspace_bytes(const boa_model* m, int n_chunks);
 /* Positions per kernel step for encode and for logits runs of 4 or more
- * positions: 4 (default; the weights and each chunk's recurrent state are read
- * once per 4 positions) or 1 (one position per step, as decode).  Outputs are
- * bit for bit the same either way.  No reference counterpart: the reference
- * codec (codec.py:56-79) always steps one position at a time. */
+ * positions.  With 4 or 8 the weights and each chunk's recurrent state are
+ * read once per 4 or 8 positions; 1 steps one position at a time, as decode.
+ * 0 (the default) lets each launch choose 4 or 8 from its chunk and position
+ * counts.  8 applies where the model's chunk tile holds whole blocks of 8
+ * (d_model 256 and 512; d_model 64 with the 16-bit kinds) and the run has 8
+ * or more positions, else 4.  Outputs are bit for bit the same for every
+ * setting.  No reference counterpart: the reference codec (codec.py:56-79)
+ * always steps one position at a time. */
 BOA_API int boa_model_set_time_block(boa_model* m, int positions);
 
 /* Wait for `stream`, then report (and clear) the device-side errors of the

@@ -153,22 +153,23 @@ def test_roundtrip_d256_split_and_single():
 @pytest.mark.parametrize("d,fmt", [(64, "tf32"), (256, "fp16"), (64, "tf32x3"), (256, "tf32x3"), (64, "f16x2"),
                                    (256, "f16x2")])
 def test_time_blocked_encode_matches_one_position_steps(d, fmt):
-    """Encode in time blocks of 4 positions (the default) writes the same
-    words as encode one position per kernel step, for lengths that end at
-    every offset inside a block; decode (always one position per step) reads
-    them back."""
+    """Encode in time blocks of 4 and of 8 positions, and with the block the
+    launch chooses (the default), writes the same words as encode one
+    position per kernel step, for lengths that end at every offset inside a
+    block; decode (always one position per step) reads them back."""
     import codec
     m = _model(d, 2, fmt)
     nm = m.native(torch.device("cuda", 0))
-    lens = [1, 2, 3, 4, 5, 6, 7, 8, 9, 63, 64, 65, 130] * 3
+    lens = [1, 2, 3, 4, 5, 6, 7, 8, 9, 15, 16, 17, 63, 64, 65, 130] * 3
     xs = _chunks(9, lens)
     nm.set_time_block(1)
     comp1, first1, Ls1 = codec.compress_GPU(m, xs)
-    nm.set_time_block(4)
-    comp4, first4, Ls4 = codec.compress_GPU(m, xs)
-    assert first1 == first4 and Ls1 == Ls4
-    assert all(np.array_equal(a, b) for a, b in zip(comp1, comp4))
-    outs = codec.decompress_GPU(m, comp4, Ls4, first4)
+    for tb in (4, 8, 0):
+        nm.set_time_block(tb)
+        comp, first, Ls = codec.compress_GPU(m, xs)
+        assert first1 == first and Ls1 == Ls
+        assert all(np.array_equal(a, b) for a, b in zip(comp1, comp)), tb
+    outs = codec.decompress_GPU(m, comp, Ls, first)
     assert all(np.array_equal(x.numpy(), o) for x, o in zip(xs, outs))
 
 

@@ -105,10 +105,15 @@ def test_logits_identical_across_decompositions(fmt):
     nm.set_time_block(4)                                             # 8 chunks x 4 positions per CTA
     got_tb = _native_logits(m, base)                                 # 6 positions: one full, one partial block
     got_tb_mid = _native_logits(m, mid)[:20]
+    nm.set_time_block(8)                                             # 4 chunks x 8 positions per CTA
+    long = rng.integers(0, 256, (20, 13)).astype(np.int64)
+    long[:, :6] = base
+    got_tb8 = _native_logits(m, long)[:, :6]                         # 13 positions: one full, one partial block
     assert torch.equal(small, got_mid)
     assert torch.equal(small, got_big)
     assert torch.equal(small, got_tb)
     assert torch.equal(small, got_tb_mid)
+    assert torch.equal(small, got_tb8)
 
 
 def test_evaluate_bpp_matches_oracle():
@@ -208,9 +213,14 @@ def test_split_kind_identical_across_decompositions(fmt):
     big = np.concatenate([base, rng.integers(0, 256, (2400 - 20, 6))])
     got_big = _native_logits(m, big)[:20]                            # 16 value columns per CTA
     nm.set_time_block(4)
-    got_tb = _native_logits(m, base)                                 # 4 chunks x 4 positions per CTA
+    got_tb = _native_logits(m, base)                                 # 2 (4) chunks x 4 positions per CTA
+    nm.set_time_block(8)
+    long = rng.integers(0, 256, (20, 13)).astype(np.int64)
+    long[:, :6] = base
+    got_tb8 = _native_logits(m, long)[:, :6]                         # 1 (2) chunks x 8 positions per CTA
     assert torch.equal(small, got_big)
     assert torch.equal(small, got_tb)
+    assert torch.equal(small, got_tb8)
 
 
 def test_f16x2_reports_activations_out_of_range():
