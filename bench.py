@@ -200,14 +200,15 @@ def measured_tensor_peak(fmt):
     return bf16, src
 
 
-def traffic_per_coded_byte(d, L, fmt, launch):
+def traffic_per_coded_byte(d, L, fmt, launch, time_block=1):
     """ncu DRAM bytes per coded byte of the decode or encode launch, for the
-    model shape and operand kind the capture was taken on (None otherwise)."""
+    model shape, operand kind and positions per kernel step the capture was
+    taken on (None otherwise)."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         for rec in json.load(open(p)).values():
             if (rec.get("model") == {"d_model": d, "num_layers": L} and rec.get("weights") == fmt
-                    and rec.get("launch") == launch):
+                    and rec.get("launch") == launch and rec.get("time_block", 1) == time_block):
                 return float(rec["dram_bytes_per_coded_byte"])
     except Exception:
         pass
@@ -470,12 +471,14 @@ def run_ours(args, cfg, rank, world, local_rank, dist):
             "traffic": (tpb * coded_timed / args.steps if tpb else None),
             "algorithmic_bytes_per_launch": alg_d / args.steps,
             "per_unit": f"{sb} B recurrent-state read+write per coded byte"}
-    # encode launch: time blocks of 4 positions read and write the state once per block
-    tb = 4
+    # encode launch: time blocks of tb positions read and write the state once
+    # per block; tb is what the library chose for a wave's segment launch
+    (w0, w1), (a0, a1) = unit(0)
+    tb = nm.time_block(w1 - w0, a1 - a0)
     alg_c = sb * coded_timed // tb + bytes_timed + 4 * words_timed
     ach_c = alg_c / t_c / 1e9
-    tpb_c = traffic_per_coded_byte(cfg["d"], cfg["L"], fmt, "encode")
-    roof_c = {"bound": "hbm", "kernel": "k_boa_step encode launch (time blocks of 4 positions)",
+    tpb_c = traffic_per_coded_byte(cfg["d"], cfg["L"], fmt, "encode", tb)
+    roof_c = {"bound": "hbm", "kernel": f"k_boa_step encode launch (time blocks of {tb} positions)",
               "achieved": ach_c, "peak": peak, "unit": "GB/s", "frac": ach_c / peak,
               "traffic": (tpb_c * coded_timed / args.steps if tpb_c else None),
               "algorithmic_bytes_per_launch": alg_c / args.steps,

@@ -61,6 +61,7 @@ SIGNATURES = {
     "boa_model_workspace_bytes": [_P, _I],
     "boa_model_info": [_P, _P, _P, _P, _P, _P],
     "boa_model_set_time_block": [_P, _I],
+    "boa_model_time_block": [_P, _I, _I, _P],
     "boa_model_status": [_P, _P],
     "boa_diag_timeout": [_I64, _I],
     "boa_diag_gemm": [_I, _I, _I, _P, _P, _P, _I],

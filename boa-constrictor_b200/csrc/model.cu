@@ -466,6 +466,29 @@ BOA_API int boa_model_set_time_block(boa_model* m, int positions) {
   return BOA_OK;
 }
 
+BOA_API int boa_model_time_block(const boa_model* m, int n_chunks, int positions, int* positions_per_step) {
+  if (!m || n_chunks < 1 || positions < 1 || !positions_per_step)
+    return boa_fail(BOA_ERR_ARG, "boa_model_time_block: bad arguments");
+  int tb = 0;
+  switch (m->D * 8 + m->kind) {
+    case 64 * 8 + 0: tb = boa::encode_time_block_t<64, 0>(m, n_chunks, positions); break;
+    case 64 * 8 + 1: tb = boa::encode_time_block_t<64, 1>(m, n_chunks, positions); break;
+    case 64 * 8 + 2: tb = boa::encode_time_block_t<64, 2>(m, n_chunks, positions); break;
+    case 64 * 8 + 3: tb = boa::encode_time_block_t<64, 3>(m, n_chunks, positions); break;
+    case 64 * 8 + 4: tb = boa::encode_time_block_t<64, 4>(m, n_chunks, positions); break;
+    case 256 * 8 + 0: tb = boa::encode_time_block_t<256, 0>(m, n_chunks, positions); break;
+    case 256 * 8 + 1: tb = boa::encode_time_block_t<256, 1>(m, n_chunks, positions); break;
+    case 256 * 8 + 2: tb = boa::encode_time_block_t<256, 2>(m, n_chunks, positions); break;
+    case 256 * 8 + 3: tb = boa::encode_time_block_t<256, 3>(m, n_chunks, positions); break;
+    case 256 * 8 + 4: tb = boa::encode_time_block_t<256, 4>(m, n_chunks, positions); break;
+    case 512 * 8 + 1: tb = boa::encode_time_block_t<512, 1>(m, n_chunks, positions); break;
+    case 512 * 8 + 2: tb = boa::encode_time_block_t<512, 2>(m, n_chunks, positions); break;
+    default: return boa_fail(BOA_ERR_UNSUPPORTED, "no kernel for this d_model / weight format");
+  }
+  *positions_per_step = tb;
+  return BOA_OK;
+}
+
 BOA_API int boa_model_info(const boa_model* m, int* d_model, int* n_layers, int* vocab, int* weight_format,
                            size_t* tile_bytes_per_step) {
   if (!m) return boa_fail(BOA_ERR_ARG, "boa_model_info: null handle");

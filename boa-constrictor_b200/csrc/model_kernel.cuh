@@ -1239,6 +1239,20 @@ inline int choose_time_block(int n_chunks, int chunks_per_cta_tb1, int positions
   return positions >= 8 && cost(8) < cost(4) ? 8 : 4;
 }
 
+// Positions per kernel step of an encode / logits launch over n_chunks chunks
+// and `positions` positions (1: one position per step).
+template <int D, int KIND>
+int encode_time_block_t(const boa_model* m, int n_chunks, int positions) {
+  if (m->time_block == 1 || positions < 4) return 1;
+  if constexpr (time_block8_ok<D, KIND>()) {
+    if (m->time_block == 0)
+      return choose_time_block(n_chunks, ChunkTileMax<D, KIND>::value / tc::OpKind<KIND>::kHiLo, positions,
+                               m->n_sms);
+    return m->time_block == 8 && positions >= 8 ? 8 : 4;
+  }
+  return 4;
+}
+
 // Pick the decomposition.  Encode and logits runs of at least 4 positions use
 // time blocks of 4 or 8 positions (choose_time_block, or the model's setting)
 // on the widest single-CTA tile (32 operand columns: 8 chunks with 16-bit
@@ -1252,14 +1266,14 @@ inline int choose_time_block(int n_chunks, int chunks_per_cta_tb1, int positions
 template <int D, int KIND>
 int launch_step_t(const boa_model* m, StepArgs& a, int n_chunks, cudaStream_t s, int positions) {
   constexpr int HL = tc::OpKind<KIND>::kHiLo;
-  if (m->time_block != 1 && positions >= 4 && (a.mode == MODE_ENCODE || a.mode == MODE_LOGITS)) {
+  const bool blocked = a.mode == MODE_ENCODE || a.mode == MODE_LOGITS;
+  const int tb = blocked ? encode_time_block_t<D, KIND>(m, n_chunks, positions) : 1;
+  if (tb > 1) {
     a.tiles_per_step = m->plan.per_step;
     a.tiles_per_layer = m->plan.per_layer;
     a.wtiles = m->d_tiles;
     constexpr int CTM = ChunkTileMax<D, KIND>::value;
     if constexpr (time_block8_ok<D, KIND>()) {
-      const int tb = m->time_block == 0 ? choose_time_block(n_chunks, CTM / HL, positions, m->n_sms)
-                                        : (m->time_block == 8 && positions >= 8 ? 8 : 4);
       if (tb == 8) return launch_step_ct<D, KIND, CTM, 1, 8>(a, n_chunks, s);
     }
     return launch_step_ct<D, KIND, CTM, 1, 4>(a, n_chunks, s);

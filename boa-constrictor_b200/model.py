@@ -121,6 +121,12 @@ class NativeModel:
         launch chooses 4 or 8), 1, 4 or 8.  The output bits are the same."""
         _n.call("boa_model_set_time_block", self.h, int(positions))
 
+    def time_block(self, n_chunks: int, positions: int) -> int:
+        """Positions per kernel step an encode / logits launch of this shape takes."""
+        tb = ctypes.c_int(0)
+        _n.call("boa_model_time_block", self.h, int(n_chunks), int(positions), ctypes.byref(tb))
+        return tb.value
+
     def check(self, stream=None) -> None:
         """Wait for `stream` (torch's current stream by default) and raise the
         device-side errors of this model's calls enqueued so far

@@ -174,6 +174,10 @@ BOA_API size_t boa_model_workspace_bytes(const boa_model* m, int n_chunks);
  * setting.  No reference counterpart: the reference codec (codec.py:56-79)
  * always steps one position at a time. */
 BOA_API int boa_model_set_time_block(boa_model* m, int positions);
+/* The positions per kernel step (1, 4 or 8) that an encode or logits launch
+ * over n_chunks chunks and `positions` positions takes with the model's
+ * setting; host-only, nothing is launched. */
+BOA_API int boa_model_time_block(const boa_model* m, int n_chunks, int positions, int* positions_per_step);
 
 /* Wait for `stream`, then report (and clear) the device-side errors of the
  * model's calls enqueued so far: BOA_ERR_TIMEOUT, BOA_ERR_OVERFLOW (a coded

@@ -173,6 +173,24 @@ def test_time_blocked_encode_matches_one_position_steps(d, fmt):
     assert all(np.array_equal(x.numpy(), o) for x, o in zip(xs, outs))
 
 
+def test_time_block_choice():
+    """The launch's choice between blocks of 4 and 8: 8 when it fills the
+    waves of CTAs better (1000 chunks of 2xFP16 at d_model 256: 1000 CTAs of
+    one chunk in 7 waves instead of 500 in 4), 4 where blocks of 8 do not fit
+    the model's chunk runs; a fixed setting wins."""
+    m = _model(256, 2, "f16x2")
+    nm = m.native(torch.device("cuda", 0))
+    assert nm.time_block(1000, 4096) == 8
+    assert nm.time_block(1000, 3) == 1
+    assert nm.time_block(16, 128) == 8                             # one wave either way: fewer steps
+    for tb in (1, 4, 8):
+        nm.set_time_block(tb)
+        assert nm.time_block(1000, 4096) == tb
+    nm.set_time_block(0)
+    small = _model(64, 2, "tf32x3").native(torch.device("cuda", 0))
+    assert small.time_block(1000, 4096) == 4                      # chunk runs of 4 columns
+
+
 def test_boafile_resume_after_interrupted_compress(tmp_path, monkeypatch):
     """BoaFile.compress appends each wave as it is coded; a run that stops
     after two waves resumes with resume=True and ends with the same file as an
