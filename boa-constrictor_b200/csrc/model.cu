@@ -131,6 +131,7 @@ static uint32_t to_tf32_bits(float f) {
 struct MTile {
   const float* W;
   int M_real, K_real, ldw, mt;
+  int ks0 = 0;       // first K slice (x_proj's second K half)
 };
 
 // Append the SW128 tile images of one GEMM's M tiles, each with n_ks K slices.
@@ -154,7 +155,7 @@ static void pack_gemm(std::vector<uint8_t>& out, const std::vector<MTile>& tiles
   for (const auto& o : order) {
     const float* W = tiles[o.first].W;
     const int M_real = tiles[o.first].M_real, K_real = tiles[o.first].K_real, ldw = tiles[o.first].ldw;
-    const int mt = tiles[o.first].mt, ks = o.second;
+    const int mt = tiles[o.first].mt, ks = tiles[o.first].ks0 + o.second;
     for (int hl = 0; hl < hl_n; ++hl) {
       const size_t base = out.size();
       out.resize(base + kTileBytes, 0);
@@ -236,7 +237,11 @@ static void pack_stream(std::vector<uint8_t>& tiles, const TilePlan& p, int rank
     add_mtiles(in, w.w_in, 2 * E, D, D, rank * p.ltE, p.ltE);
     add_mtiles(in, w.w_in, 2 * E, D, D, p.mtE + rank * p.ltE, p.ltE);
     pack_gemm(tiles, in, p.kD, kind, pairs);
-    gemm(w.w_x, DBC, E, E, 0, 1, p.kE);
+    std::vector<MTile> xp;                                                   // M tile 0 as two K halves
+    add_mtiles(xp, w.w_x, DBC, E, E, 0, 1);
+    add_mtiles(xp, w.w_x, DBC, E, E, 0, 1);
+    xp[1].ks0 = p.kE / 2;
+    pack_gemm(tiles, xp, p.kE / 2, kind, pairs);
     gemm(w.w_dt, E, R, R, rank * p.ltE, p.ltE, 1);
     gemm(w.w_out, D, E, E, rank * p.ltD, p.ltD, p.kE);
     gemm(w.w1, F, D, D, rank * p.ltF, p.ltF, p.kD);

@@ -313,7 +313,9 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
   // tiles owned by this CTA
   constexpr int LT_E = MT_E / SPLIT, LT_D = MT_D / SPLIT, LT_F = MT_F / SPLIT, LT_V = 2 / SPLIT;
   static_assert(SPLIT == 1 || (MT_E % 2 == 0 && MT_D % 2 == 0), "split needs an even number of tiles");
-  constexpr int COL_X = 0, COL_Z = LT_E * CT, COL_XP = 2 * LT_E * CT, COL_DT = COL_XP + CT;
+  // x_proj has one M tile; its K runs as two halves into two accumulators
+  // (COL_XP, COL_XP + CT), one per MMA issuer, summed in the epilogue
+  constexpr int COL_X = 0, COL_Z = LT_E * CT, COL_XP = 2 * LT_E * CT, COL_DT = COL_XP + 2 * CT;
   static_assert(COL_DT + LT_E * CT <= 512, "TMEM budget");
   static_assert(LT_F * CT <= 512, "TMEM budget (ff.0)");
   static_assert(R <= PER && DBC <= 64, "x_proj outputs must fit one tile / one K slice");
@@ -541,7 +543,8 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
       // the hi tile by rows [0, 2 VC) and the lo' tile by rows [2 VC, 4 VC).
       // tiles: also commit after every M tile (pair), so the epilogue of a
       // finished tile can start while later tiles run (in_proj -> conv, ff.0 -> GELU)
-      auto gemm = [&](int n_mt, int n_ks, int col0, bool tiles, int b_off) -> bool {
+      // b_mt: operand K slices between consecutive M tiles (x_proj's two K halves)
+      auto gemm = [&](int n_mt, int n_ks, int col0, bool tiles, int b_off, int b_mt) -> bool {
         const uint64_t bdesc0 = bdesc_base + (uint64_t)(gemm_no % S::NBUF) * kBufDesc + (uint64_t)b_off * kSliceDesc;
         constexpr int kGroup = SPLIT == 1 ? 2 : 1;          // M tiles whose K slices interleave
         for (int m0 = 0; m0 < n_mt; m0 += kGroup) {
@@ -555,7 +558,8 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
                 if (kIssuers == 1 || (mt & 1) == p) {
                   // kind 4: the lo' tile takes operand rows [2 VC, 4 VC) into columns [VC, 3 VC)
                   const uint32_t dc = tmem + (uint32_t)(col0 + mt * CT + (HL == 4 && hl ? VC : 0));
-                  const uint64_t bo = (HL == 4 && hl) ? (uint64_t)((2 * VC * 128) >> 4) : 0ull;
+                  const uint64_t bo = ((HL == 4 && hl) ? (uint64_t)((2 * VC * 128) >> 4) : 0ull) +
+                                      (uint64_t)(mt * b_mt) * kSliceDesc;
                   if (!tile_mma(dc, bd + bo, ks > 0 || hl > 0)) return false;
                 }
                 next_tile();
@@ -568,7 +572,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
         }
         return true;
       };
-      auto step_gemm = [&](int n_mt, int n_ks, int col0, bool tiles = false, int b_off = 0) -> bool {
+      auto step_gemm = [&](int n_mt, int n_ks, int col0, bool tiles = false, int b_off = 0, int b_mt = 0) -> bool {
         const long long tw = prof ? clock64() : 0;
         const bool got = SPLIT == 2 ? mbar_wait_cluster(act_bar, act_phase, abort_flag, kWaitBudget)
                                     : tc::mbar_wait(act_bar, act_phase, abort_flag, kWaitBudget);
@@ -576,7 +580,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
         if (prof) w_act += clock64() - tw;
         act_phase ^= 1u;
         tc::tc_fence_after();
-        if (!gemm(n_mt, n_ks, col0, tiles, b_off)) return false;
+        if (!gemm(n_mt, n_ks, col0, tiles, b_off, b_mt)) return false;
         tc::mma_commit(mma_bar);                            // one of the kIssuers arrivals that end the GEMM
         ++gemm_no;
         return true;
@@ -584,7 +588,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
       for (int s = 0; s < nsteps && ok; ++s) {
         for (int l = 0; l < L && ok; ++l) {
           ok = step_gemm(2 * LT_E, kD, 0, true)    // in_proj -> x | z (own channels)
-               && step_gemm(1, kE, COL_XP, false, kXOff)   // x_proj (whole)
+               && step_gemm(2, kE / 2, COL_XP, false, kXOff, kE / 2)   // x_proj (whole), two K halves
                && step_gemm(LT_E, 1, COL_DT)       // dt_proj (own channels)
                && step_gemm(LT_D, kE, 0)           // out_proj (own features)
                && step_gemm(LT_F, kD, 0, true)     // ff.0
@@ -840,8 +844,11 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
           if (g == 0) {
 #pragma unroll 1
             for (int gi = 0; gi < NG; ++gi) {
-              float v[8];
-              ldv8((uint32_t)(COL_XP + 8 * gi), v);
+              float v[8], v2[8];
+              ldv8((uint32_t)(COL_XP + 8 * gi), v);          // K half 0
+              ldv8((uint32_t)(COL_XP + CT + 8 * gi), v2);    // K half 1
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[j] += v2[j];
               if (row < DBC) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) dbc[(8 * gi + j) * 64 + row] = v[j];
