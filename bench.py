@@ -2,7 +2,7 @@
 """Benchmark of the BoaConstrictor compress/decompress hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
-                    [--segment S] [--scaling weak|strong] [--weights tf32x3|tf32|fp16|bf16]
+                    [--segment S] [--scaling weak|strong] [--weights f16x2|tf32x3|tf32|fp16|bf16]
 
 Default workload: configuration 2 of the benchmark spec -- 64 MiB of seeded
 HEP-like event records, chunks_count = 1000 (67,109 B per chunk), the
