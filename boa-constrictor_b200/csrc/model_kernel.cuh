@@ -59,12 +59,20 @@
 namespace boa {
 
 constexpr int kTileBytes = 16384;      // one A tile: 128 rows x 128 bytes
-constexpr int kComputeThreads = 512;   // warps 2..17
+// Threads per CTA: five warpgroups.  Warpgroup 0 holds the weight producer
+// (warp 0), the MMA issuer (warp 1), in single-CTA kernels a second issuer
+// (warp 2), and an idle warp; warpgroups 1-4 are the 16 compute warps.  The
+// block launches with kRegsLaunch registers a thread; warpgroup 0 then gives
+// all but kRegsCtl of them back (setmaxnreg) and the compute warpgroups take
+// them, so the epilogues, the scan and the coder run with kRegsCompute.
+constexpr int kComputeThreads = 512;   // warps 4..19
 constexpr int kComputeWarps = kComputeThreads / 32;
-constexpr int kIssuer2Warp = 18;       // second MMA issuer (single-CTA kernels)
-// Threads per CTA: producer warp, MMA warp, 16 compute warps, and in the
-// single-CTA kernels a second MMA-issuing warp.
-__host__ __device__ constexpr int threads_for(int split) { return split == 1 ? 608 : 576; }
+constexpr int kComputeWarp0 = 4;       // first compute warp
+constexpr int kIssuer2Warp = 2;        // second MMA issuer (single-CTA kernels)
+__host__ __device__ constexpr int threads_for(int) { return 640; }
+constexpr int kRegsLaunch = 96, kRegsCtl = 64, kRegsCompute = 104;
+static_assert(kRegsCtl * 128 + kRegsCompute * kComputeThreads == kRegsLaunch * 640,
+              "the warpgroups' register shares must add up to the launch's");
 constexpr long long kWaitBudget = 4000000000LL;  // SM clock cycles per bounded wait (~2 s)
 
 enum StepMode : int { MODE_ENCODE = 0, MODE_DECODE = 1, MODE_LOGITS = 2 };
@@ -447,6 +455,8 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
   const uint32_t tmem = *tmem_slot;
   const int nsteps = *nsteps_sh;
 
+  if (warp < kComputeWarp0) {
+  tc::setmaxnreg_dec<kRegsCtl>();                         // every warp of warpgroup 0
   if (warp == 0) {
     // ============================== producer ==============================
     // A bulk copy issued by one thread takes about 470 SM cycles whatever its
@@ -611,9 +621,11 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
         if (clock64() - t0 > kWaitBudget) break;
       }
     }
+  }
   } else {
+    tc::setmaxnreg_inc<kRegsCompute>();                   // every compute warp
     // ============================ compute warps ============================
-    const int ct = tid - 64;                 // 0..511
+    const int ct = tid - 32 * kComputeWarp0; // 0..511
     const int cw = ct >> 5;                  // compute warp 0..15
     const int q = warp & 3;                  // TMEM lane quarter this warp may access
     const int g = cw >> 2;                   // group 0..3 (covers all four quarters)
@@ -1199,6 +1211,14 @@ int launch_step_ct(StepArgs& a, int n_chunks, cudaStream_t s) {
   constexpr int VC = CT / tc::OpKind<KIND>::kHiLo;
   const int smem = Smem<D, KIND, CT, SPLIT>::ALLOC;
   auto kern = k_boa_step<D, KIND, CT, SPLIT, TB>;
+  // The warpgroups' setmaxnreg shares add up to kRegsLaunch registers a thread
+  // at launch; with fewer the compute warps' increase could never be granted.
+  static const int launch_regs = [&] {
+    cudaFuncAttributes fa{};
+    return cudaFuncGetAttributes(&fa, kern) == cudaSuccess ? fa.numRegs : -1;
+  }();
+  if (launch_regs != kRegsLaunch)
+    return boa_fail(BOA_ERR_UNSUPPORTED, "k_boa_step: unexpected register allocation for the warpgroup split");
   BOA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int grid = cdiv(n_chunks, VC / TB) * SPLIT;
   if constexpr (SPLIT == 1) {

@@ -90,6 +90,18 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
+// Per-warpgroup register budget (all four warps of a warpgroup execute the
+// same instruction); an increase waits until other warpgroups' decreases have
+// returned the registers to the block's launch allocation.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Make this thread's generic-proxy shared-memory writes visible to the async
 // proxy (tensor core operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
