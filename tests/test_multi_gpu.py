@@ -21,7 +21,8 @@ def _chunks(seed, lens):
 
 
 @need2
-@pytest.mark.parametrize("d,L,fmt", [(64, 2, "tf32x3"), (256, 8, "tf32x3"), (256, 2, "fp16")])
+@pytest.mark.parametrize("d,L,fmt", [(64, 2, "tf32x3"), (256, 8, "tf32x3"), (256, 8, "f16x2"), (64, 2, "f16x2"),
+                                     (256, 2, "fp16")])
 def test_encode_on_gpu0_decode_on_last_gpu(d, L, fmt):
     """Configuration 3's cross-GPU round trip: encode on GPU 0, decode on the
     box's last GPU (GPU 7 on an 8-GPU box), and re-encode there to the same
