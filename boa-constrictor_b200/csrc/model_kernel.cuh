@@ -204,9 +204,15 @@ struct Smem {
   static constexpr int o_prof = o_misc + 64;                 // PF_SLOTS x u64 phase accumulators
   static constexpr int o_ring = ((o_prof + 256 + 1023) / 1024) * 1024;
   static constexpr int kBudget = 227 * 1024 - 1024;          // minus alignment slack
-  static constexpr int STAGES_FIT = (kBudget - o_ring) / kTileBytes;
+  // The split kinds take each (M tile, K slice) as a hi tile and a lo tile,
+  // consecutive in the weight stream and multiplied by the same issuer: a
+  // ring slot then holds the pair (one wait, 8 MMAs, one release), where at
+  // least 4 pair slots fit.
+  static constexpr bool PAIR = tc::OpKind<KIND>::kHiLo >= 2 && (kBudget - o_ring) / (2 * kTileBytes) >= 4;
+  static constexpr int SLOT = (PAIR ? 2 : 1) * kTileBytes;
+  static constexpr int STAGES_FIT = (kBudget - o_ring) / SLOT;
   static constexpr int STAGES = STAGES_FIT > kMaxStages ? kMaxStages : STAGES_FIT;
-  static constexpr int TOTAL = o_ring + STAGES * kTileBytes;
+  static constexpr int TOTAL = o_ring + STAGES * SLOT;
   static constexpr int ALLOC = TOTAL + 1024;
   static_assert(STAGES >= 3, "not enough shared memory for the weight ring");
 };
@@ -463,12 +469,13 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
     // size up to 64 KB, and a thread's copies do not overlap, so one lane
     // streaming 16 KB tiles delivers ~35 B/clk on its own.  kProducers lanes
     // each own the ring slots st with st % kProducers == lane and fill them in
-    // tile order, so the copies of different lanes overlap.  Measured at
+    // slot order, so the copies of different lanes overlap.  Measured at
     // d_model 256 / 8 layers and 1000 chunks: two lanes shorten 2xFP16 encode
     // and decode steps by about 5 % and 3xTF32 decode steps by 9 %, but
     // lengthen 3xTF32 encode steps by 13 % and leave fp16 unchanged; three
-    // lanes are slower than two, and 32 / 64 KB copies of 2 / 4 tiles gain
-    // nothing.
+    // lanes are slower than two.  Pair slots (S::PAIR, one 32 KB copy of a hi
+    // and a lo tile) shortened 2xFP16 encode steps by a further 13 % and
+    // decode steps by 6 %: they halve the issuers' waits and releases.
     if (lane < kProducers && nsteps > 0) {
       const uint64_t pol = tc::policy_evict_last();
       bool ok = true;
@@ -479,18 +486,19 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
 #endif
       unsigned long long w_empty = 0;
       const uint8_t* base = a.wtiles + (long long)rank * a.tiles_per_step * kTileBytes;
-      const long long total = (long long)nsteps * a.tiles_per_step;
+      const int slots_per_step = a.tiles_per_step / (S::PAIR ? 2 : 1);
+      const long long total = (long long)nsteps * slots_per_step;
       for (long long r = 0; ok; ++r) {                     // ring rounds
         for (int st = lane; st < kStagesK; st += kProducers) {
-          const long long g = r * kStagesK + st;           // tile index in consumption order
+          const long long g = r * kStagesK + st;           // slot-load index in consumption order
           if (g >= total) { ok = false; break; }
           const long long tw = prof ? clock64() : 0;
           if (!tc::mbar_wait(&empty[st], (uint32_t)(r & 1) ^ 1u, abort_flag, kWaitBudget)) { ok = false; break; }
           if (prof) w_empty += clock64() - tw;
           if constexpr (kIssuers == 2) slot_tile[st] = (uint16_t)g;
           slot_ph[st] = (uint8_t)(r & 1);
-          tc::mbar_arrive_expect_tx(&full[st], kTileBytes);
-          tc::bulk_g2s(ring + st * kTileBytes, base + (g % a.tiles_per_step) * kTileBytes, kTileBytes, &full[st], pol);
+          tc::mbar_arrive_expect_tx(&full[st], S::SLOT);
+          tc::bulk_g2s(ring + st * S::SLOT, base + (g % slots_per_step) * S::SLOT, S::SLOT, &full[st], pol);
         }
       }
       if (prof) a.prof[PF_PROD_WAIT_EMPTY] = w_empty;
@@ -503,6 +511,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
       const uint32_t id = tc::idesc<KIND>(128, HL == 4 ? CT / 2 : CT);
       const uint64_t adesc0 = tc::sdesc_sw128(tc::smem_u32(ring));
       constexpr uint64_t kTileDesc = kTileBytes >> 4;      // descriptor start-address units (16 B)
+      constexpr uint64_t kSlotDesc = S::SLOT >> 4;
       constexpr uint64_t kSliceDesc = (CT * 128) >> 4;
       constexpr uint64_t kBufDesc = S::BBUF >> 4;
       const uint64_t bdesc_base = tc::sdesc_sw128(tc::smem_u32(bbuf0));
@@ -519,8 +528,10 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
 #endif
       unsigned long long w_full = 0, w_act = 0;
       const long long t_mma0 = clock64();
-      // One weight tile: wait for it, issue its four K8 / K16 MMAs, release the slot.
-      auto tile_mma = [&](uint32_t dcol, uint64_t bd, bool acc) -> bool {
+      // One ring slot: wait for it, issue the four K8 / K16 MMAs of its tile
+      // (with pair slots, then the four of its lo tile into dcol2 with bd2),
+      // release the slot.
+      auto tile_mma = [&](uint32_t dcol, uint64_t bd, bool acc, uint32_t dcol2 = 0, uint64_t bd2 = 0) -> bool {
         const long long tw = prof ? clock64() : 0;
         if constexpr (kIssuers == 2) {                     // the producer has moved this slot on to tile `it`
           const long long t0 = clock64();
@@ -532,11 +543,18 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
         if (!tc::mbar_wait(&full[st], ph, abort_flag, kWaitBudget)) return false;
         if (prof) w_full += clock64() - tw;
         tc::tc_fence_after();
-        const uint64_t ad = adesc0 + (uint64_t)st * kTileDesc;
+        const uint64_t ad = adesc0 + (uint64_t)st * kSlotDesc;
         tc::mma<KIND>(dcol, ad, bd, id, acc ? 1u : 0u);
         tc::mma<KIND>(dcol, ad + 2, bd + 2, id, 1u);       // +32 bytes of K
         tc::mma<KIND>(dcol, ad + 4, bd + 4, id, 1u);
         tc::mma<KIND>(dcol, ad + 6, bd + 6, id, 1u);
+        if constexpr (S::PAIR) {                           // the lo tile, 16 KB further on
+          const uint64_t al = ad + kTileDesc;
+          tc::mma<KIND>(dcol2, al, bd2, id, 1u);
+          tc::mma<KIND>(dcol2, al + 2, bd2 + 2, id, 1u);
+          tc::mma<KIND>(dcol2, al + 4, bd2 + 4, id, 1u);
+          tc::mma<KIND>(dcol2, al + 6, bd2 + 6, id, 1u);
+        }
         tc::mma_commit(&empty[st]);
         return true;
       };
@@ -563,16 +581,21 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
           for (int ks = 0; ks < n_ks; ++ks, bd += kSliceDesc) {
             for (int h = 0; h < nm; ++h) {
               const int mt = m0 + h;
-#pragma unroll
-              for (int hl = 0; hl < (HL == 1 ? 1 : 2); ++hl) {
-                if (kIssuers == 1 || (mt & 1) == p) {
-                  // kind 4: the lo' tile takes operand rows [2 VC, 4 VC) into columns [VC, 3 VC)
-                  const uint32_t dc = tmem + (uint32_t)(col0 + mt * CT + (HL == 4 && hl ? VC : 0));
-                  const uint64_t bo = ((HL == 4 && hl) ? (uint64_t)((2 * VC * 128) >> 4) : 0ull) +
-                                      (uint64_t)(mt * b_mt) * kSliceDesc;
-                  if (!tile_mma(dc, bd + bo, ks > 0 || hl > 0)) return false;
-                }
+              // kind 4: the lo' tile takes operand rows [2 VC, 4 VC) into columns [VC, 3 VC)
+              const uint32_t dc_hi = tmem + (uint32_t)(col0 + mt * CT);
+              const uint32_t dc_lo = dc_hi + (HL == 4 ? (uint32_t)VC : 0u);
+              const uint64_t bd_hi = bd + (uint64_t)(mt * b_mt) * kSliceDesc;
+              const uint64_t bd_lo = bd_hi + (HL == 4 ? (uint64_t)((2 * VC * 128) >> 4) : 0ull);
+              const bool mine = kIssuers == 1 || (mt & 1) == p;
+              if constexpr (S::PAIR) {
+                if (mine && !tile_mma(dc_hi, bd_hi, ks > 0, dc_lo, bd_lo)) return false;
                 next_tile();
+              } else {
+#pragma unroll
+                for (int hl = 0; hl < (HL == 1 ? 1 : 2); ++hl) {
+                  if (mine && !tile_mma(hl ? dc_lo : dc_hi, hl ? bd_lo : bd_hi, ks > 0 || hl > 0)) return false;
+                  next_tile();
+                }
               }
             }
           }
