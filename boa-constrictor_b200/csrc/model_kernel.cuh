@@ -20,19 +20,21 @@
 // splitting the output features) owns CT operand columns and runs every
 // timestep of every layer for them; clusters never talk to each other because
 // the whole step is row-local per chunk.  A value column is one chunk, or, in
-// the time-blocked encode / logits form (TB = 4), one of TB consecutive
-// positions of a chunk.  With the split operand kind (3xTF32) every value
-// column occupies two operand columns (its tf32 hi and lo halves), so a tile
-// of CT operand columns holds CT / 2 value columns.  Roles inside the CTA:
+// the time-blocked encode / logits form, one of TB consecutive positions of
+// a chunk (TB = 4 or 8).  With the split operand kinds every
+// value column occupies two (3xTF32: tf32 hi and lo) or four (2xFP16: hi, lo',
+// hi, zero) operand rows, so a tile of CT operand columns holds CT / 2 or
+// CT / 4 value columns.  Roles inside the CTA (five warpgroups):
 //   warp 0      streams every projection weight tile (pre-packed 16 KB SW128
 //               images, in consumption order) through a shared-memory ring
 //               with bulk async copies;
 //   warp 1      allocates TMEM and issues tcgen05.mma: weights are the A
 //               operand (M = 128 output features per tile), the chunks'
 //               activations the B operand (N = CT), accumulators in TMEM;
-//   warp 18     (single-CTA kernels) a second issuer: the M tiles of every
-//               GEMM alternate between warps 1 and 18;
-//   warps 2-17  (512 threads) run the LayerNorms, conv/scan/gate, MLP and head
+//   warp 2      (single-CTA kernels) a second issuer: the M tiles of every
+//               GEMM alternate between warps 1 and 2;
+//   warp 3      idle (completes warpgroup 0);
+//   warps 4-19  (512 threads) run the LayerNorms, conv/scan/gate, MLP and head
 //               epilogues straight out of TMEM, write the next B operand into
 //               shared memory, and run quantiser + range coder (a warp per chunk).
 // The recurrent state (conv window + SSM state, fp32) streams from HBM once
