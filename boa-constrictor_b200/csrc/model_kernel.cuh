@@ -306,9 +306,12 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
   static_assert(VC % 8 == 0 && VC <= 32, "value columns");
   constexpr int NG = VC / 8;                             // groups of 8 value columns
   constexpr int kStagesK = S::STAGES;
-  // copy lanes of warp 0: two where measured faster (2xFP16 encode and decode,
-  // 3xTF32 decode), else one
-  constexpr int kProdWant = BOA_TILE_PRODUCERS > 0 ? BOA_TILE_PRODUCERS : ((KIND == 4 || (KIND == 3 && TB == 1)) ? 2 : 1);
+  // copy lanes of warp 0: one with pair slots (32 KB copies) and in general;
+  // two where measured faster with 16 KB slots (2xFP16, 3xTF32 decode)
+  constexpr int kProdWant = BOA_TILE_PRODUCERS > 0 ? BOA_TILE_PRODUCERS
+                            : S::PAIR                         ? 1
+                            : (KIND == 4 || (KIND == 3 && TB == 1)) ? 2
+                                                                    : 1;
   constexpr int kProducers = kStagesK < kProdWant ? kStagesK : kProdWant;
   // Issuing a tcgen05.mma costs the issuing thread about as long as the tensor
   // core needs for it at N <= 64, so single-CTA kernels (whose GEMMs have two
@@ -477,7 +480,9 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
     // lengthen 3xTF32 encode steps by 13 % and leave fp16 unchanged; three
     // lanes are slower than two.  Pair slots (S::PAIR, one 32 KB copy of a hi
     // and a lo tile) shortened 2xFP16 encode steps by a further 13 % and
-    // decode steps by 6 %: they halve the issuers' waits and releases.
+    // decode steps by 6 %: they halve the issuers' waits and releases.  With
+    // pair slots one lane is faster again than two (2xFP16: encode 4 %,
+    // decode 6 %), so pair-slot kernels take one.
     if (lane < kProducers && nsteps > 0) {
       const uint64_t pol = tc::policy_evict_last();
       bool ok = true;
