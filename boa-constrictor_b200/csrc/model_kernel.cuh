@@ -742,7 +742,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
       }
       ++gemm_no;
     };
-    // Wait for the GEMM just issued; the verdict is uniform over the 512 threads.
+    // Wait for the GEMM just issued; the result is uniform over the 512 threads.
     auto wait_mma = [&]() -> bool {
       tc::mbar_wait(mma_bar, mma_phase, abort_flag, kWaitBudget);
       mma_phase ^= 1u;
@@ -766,7 +766,7 @@ __global__ void __launch_bounds__(threads_for(SPLIT), 1) k_boa_step(const __grid
       tc::tc_fence_after();
     };
     // After writing shared values into the peer: tell it, then wait for its
-    // values to have arrived here.  Uniform verdict as wait_mma.
+    // values to have arrived here.  Uniform result as wait_mma.
     auto exchange = [&]() -> bool {
       if constexpr (SPLIT == 2) {
         __syncwarp();
