@@ -27,3 +27,18 @@ def test_library_exports_all_declared_symbols():
 
 def test_bindings_cover_header():
     assert declared_symbols() <= set(_native.SIGNATURES)
+
+
+def test_python_constants_match_header():
+    """Status codes, quantiser modes and operand kinds: the Python binding's
+    values are the header's."""
+    txt = open(os.path.join(ROOT, "include", "boa_b200.h")).read()
+    defs = dict(re.findall(r"#define\s+(BOA_(?:OK|ERR_\w+|QUANT_\w+|WEIGHTS_\w+))\s+(\d+)", txt))
+    assert len(defs) >= 14
+    for name, value in defs.items():
+        assert getattr(_native, name) == int(value), name
+    import model
+    import boa_b200.container as C
+    # every operand kind has a Python name and a container code
+    assert set(model.WEIGHT_FORMATS.values()) == {int(v) for k, v in defs.items() if k.startswith("BOA_WEIGHTS_")}
+    assert set(C.WEIGHT_FORMAT_CODES) == set(model.WEIGHT_FORMATS)
